@@ -1,0 +1,103 @@
+/*
+ * bsattn.h -- C ABI of the B200 (sm_100a) block-sparse causal attention forward.
+ *
+ * This library replaces the Python/Triton entry point of sissississi-013/usagi:
+ *
+ *   block_sparse_attn_fwd(q, k, v, row_ptr, col_idx, seq_lens) -> (o, lse)
+ *       kernels/v4_leaderboard_0740ms.py:242-243  (same in v7 :251-252, v1 :504-505)
+ *   _run_csr(...)  host glue: flatten to [B*H, T, D], int32 metadata, grid launch
+ *       kernels/v4_leaderboard_0740ms.py:143-179
+ *   _fwd_csr(...)  the Triton device kernel
+ *       kernels/v4_leaderboard_0740ms.py:31-136
+ *   setup(suite_specs, device, variants)  precompiles Triton variants
+ *       kernels/v4_leaderboard_0740ms.py:189-238  (nothing to precompile here: the kernel is
+ *       built ahead of time for sm_100a; bsattn_setup only checks the device)
+ *   PythonCudaLauncher.__call__  ctypes cuLaunchKernel launcher, RuntimeError on failure
+ *       kernels/v1_baseline.py:75-130  (replaced by bsattn_fwd's own launch + return codes)
+ *
+ * Conventions
+ *   - All tensor pointers are DEVICE pointers of the current CUDA device.
+ *   - q, k, v, o are contiguous [B, H, T, D] with D == 128 and T % 128 == 0, 16-byte aligned.
+ *   - row_ptr: int32, for head bh = b*H + h its nqb+1 offsets start at row_ptr + bh*rp_stride_bh
+ *     (rp_stride_bh may be 0 to share one pattern across all heads).
+ *   - col_idx: int32, head bh's column list starts at col_idx + bh*ci_stride_bh and holds
+ *     max_nnz entries (ci_stride_bh may be 0).
+ *   - seq_lens: int32 [B] valid length per batch entry, or NULL for "all T".
+ *   - lse: float32 [B, H, T] natural-log logsumexp, or NULL to skip it.
+ *   - stream: a cudaStream_t passed as void* (NULL = legacy default stream).
+ *   - Calls are asynchronous on `stream`; nothing is allocated and nothing synchronises.
+ *   - Functions return 0 on success or a negative BSATTN_E* code.
+ */
+#ifndef USAGI_B200_BSATTN_H
+#define USAGI_B200_BSATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define BSATTN_API __attribute__((visibility("default")))
+#else
+#define BSATTN_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  BSATTN_OK = 0,
+  BSATTN_E_SHAPE = -1,      /* B, H, T or D out of range, T % 128 != 0, D != 128          */
+  BSATTN_E_ALIGN = -2,      /* q/k/v/o not 16-byte aligned                                  */
+  BSATTN_E_NULL = -3,       /* required pointer is NULL                                     */
+  BSATTN_E_WORKSPACE = -4,  /* workspace NULL or smaller than bsattn_workspace_bytes()      */
+  BSATTN_E_CUDA = -5,       /* CUDA runtime error (launch, attribute, device query)         */
+  BSATTN_E_TMA = -6,        /* cuTensorMapEncodeTiled unavailable or failed                 */
+  BSATTN_E_DEVICE = -7,     /* current device is not an sm_100 part                         */
+  BSATTN_E_CSR = -8,        /* (device-reported) CSR row or column index out of range       */
+  BSATTN_E_TIMEOUT = -9,    /* (device-reported) a pipeline wait exceeded its time limit    */
+  BSATTN_E_DTYPE = -10      /* unsupported dtype code                                       */
+};
+
+/* Output element type of `o`. */
+enum { BSATTN_OUT_F16 = 0, BSATTN_OUT_BF16 = 1 };
+
+/* Bytes of device workspace bsattn_fwd needs (error word, scheduler state). Zero it once
+ * before first use (cudaMemset); the kernel leaves it ready for the next call. One workspace
+ * per concurrently running stream. */
+BSATTN_API size_t bsattn_workspace_bytes(void);
+
+/* Forward pass: o = softmax(q k^T * scale, CSR block mask, causal diagonal) v.
+ * Replaces block_sparse_attn_fwd / _run_csr / _fwd_csr (kernels/v4_leaderboard_0740ms.py:31-243).
+ * scale <= 0 selects 1/sqrt(D) (the reference's fixed _SCORE_SCALE, v4 :19). */
+BSATTN_API int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+               const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens,
+               int B, int H, int T, int D,
+               int64_t rp_stride_bh, int64_t ci_stride_bh, int max_nnz,
+               float scale, int out_dtype,
+               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Reads and clears the device error word of `workspace` (synchronises `stream`).
+ * *status receives 0, BSATTN_E_CSR or BSATTN_E_TIMEOUT. Replaces the RuntimeError the
+ * reference's launcher raised on a failed launch (kernels/v1_baseline.py:126-128). */
+BSATTN_API int bsattn_check_error(void* workspace, void* stream, int* status);
+
+/* Checks that the current device can run the kernel and configures it (shared-memory
+ * carve-out). Idempotent. Counterpart of setup() (kernels/v4_leaderboard_0740ms.py:189-238). */
+BSATTN_API int bsattn_setup(void);
+
+/* Upper bound on a pipeline wait inside the kernel, in nanoseconds (default 2e9).
+ * A wait that exceeds it makes the kernel stop, free its tensor memory and report
+ * BSATTN_E_TIMEOUT through bsattn_check_error. Applies to later launches in this process. */
+BSATTN_API void bsattn_set_timeout_ns(uint64_t ns);
+
+/* Human-readable text for a BSATTN_E* code. */
+BSATTN_API const char* bsattn_strerror(int code);
+
+/* ABI version of this header (major*100 + minor). */
+BSATTN_API int bsattn_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* USAGI_B200_BSATTN_H */

@@ -1,0 +1,68 @@
+"""ctypes binding of ``libbsattn.so`` -- the C ABI declared in ``include/bsattn.h``.
+
+There is no fallback: if the library is missing or does not export the ABI, loading raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+from .build import LIB_PATH
+
+_c_int, _c_void_p, _c_size_t = ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t
+
+# name -> (restype, argtypes); must match include/bsattn.h
+SIGNATURES = {
+    "bsattn_workspace_bytes": (_c_size_t, []),
+    "bsattn_version": (_c_int, []),
+    "bsattn_set_timeout_ns": (None, [ctypes.c_uint64]),
+    "bsattn_setup": (_c_int, []),
+    "bsattn_strerror": (ctypes.c_char_p, [_c_int]),
+    "bsattn_fwd": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p,          # q, k, v
+        _c_void_p, _c_void_p,                     # o, lse
+        _c_void_p, _c_void_p, _c_void_p,          # row_ptr, col_idx, seq_lens
+        _c_int, _c_int, _c_int, _c_int,           # B, H, T, D
+        ctypes.c_int64, ctypes.c_int64, _c_int,   # rp_stride_bh, ci_stride_bh, max_nnz
+        ctypes.c_float, _c_int,                   # scale, out_dtype
+        _c_void_p, _c_size_t, _c_void_p,          # workspace, bytes, stream
+    ]),
+    "bsattn_check_error": (_c_int, [_c_void_p, _c_void_p, ctypes.POINTER(_c_int)]),
+}
+
+# error codes (include/bsattn.h)
+OK = 0
+E_SHAPE, E_ALIGN, E_NULL, E_WORKSPACE, E_CUDA, E_TMA, E_DEVICE, E_CSR, E_TIMEOUT, E_DTYPE = (
+    -1, -2, -3, -4, -5, -6, -7, -8, -9, -10)
+OUT_F16, OUT_BF16 = 0, 1
+
+_lock = threading.Lock()
+_lib = None
+
+
+def library_path() -> Path:
+    return LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load the in-tree kernel library once; raise if it is absent (no CPU fallback)."""
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not LIB_PATH.exists():
+            raise RuntimeError(
+                f"{LIB_PATH} is missing; build it with `python -m usagi_b200.build` "
+                "(the block-sparse attention path has no non-CUDA fallback)")
+        lib = ctypes.CDLL(str(LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)  # AttributeError if the ABI is incomplete
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+        return lib
+
+
+def strerror(code: int) -> str:
+    return load().bsattn_strerror(int(code)).decode()
