@@ -1,0 +1,444 @@
+"""Benchmark: block-sparse causal attention forward on B200.
+
+Metric: ms/call and live-block TFLOP/s at B=2, H=16, T=8192, D=128 against the
+B200 fp16 tensor-core peak.  One *step* = one call for each of the three sparsity families
+(sliding window 8, global prefix 4 + window 4, retrieval 8 random), fp16 inputs ~N(0,1),
+synthetic (seeded) data.  ``value`` is whole-job live-block TFLOP/s = live tiles x 4*128^3 FLOP
+summed over the three calls and all ranks, divided by the max-over-ranks device time.
+
+Multi-GPU: one process per GPU (torchrun); every rank runs the same per-GPU workload on its own
+(batch, head) shard -- B = 2 per rank of a global batch 2N -- with no collective on the data path
+(weak scaling).  The optional NCCL gather of o to rank 0 is timed separately (``gather_ms``).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+``--impl reference`` times the reference's CPU path (the dense-masked fp32 restatement in
+oracle/, the reference having no CPU implementation of its own) on the host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import torch
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+FAMILIES = ["window8", "prefix4+window4", "retrieval8"]
+B_PER_RANK, H, T, D = 2, 16, 8192, 128
+METRIC = "ms/call + live-block TFLOP/s (B=2,H=16,T=8192,D=128) vs B200 fp16 TC peak"
+FALLBACK_PEAKS = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "source": "fallback"}
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"bf16_tflops": float(d["bf16_tflops"]), "hbm_gbs": float(d["hbm_gbs"]),
+                "source": "measured"}
+    except Exception:
+        return dict(FALLBACK_PEAKS)
+
+
+def load_traffic():
+    """Per-launch DRAM bytes of the kernel from the committed ncu summary (or None)."""
+    path = os.path.join(ROOT, "profiles", "bsattn_fwd_traffic.txt")
+    try:
+        out = {}
+        with open(path) as f:
+            for line in f:
+                if ":" in line and not line.startswith("#"):
+                    k, v = line.split(":", 1)
+                    out[k.strip()] = v.strip()
+        return out
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self._t = threading.Thread(target=self._read, daemon=True)
+            self._t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": mx, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def make_inputs(device, rank, fam):
+    from usagi_b200 import patterns as P
+    g = torch.Generator(device=device).manual_seed(1000 * rank + FAMILIES.index(fam))
+    shape = (B_PER_RANK, H, T, D)
+    q = torch.randn(shape, generator=g, device=device, dtype=torch.float32).half()
+    k = torch.randn(shape, generator=g, device=device, dtype=torch.float32).half()
+    v = torch.randn(shape, generator=g, device=device, dtype=torch.float32).half()
+    pat = P.family_pattern(fam, B_PER_RANK, H, T)
+    return q, k, v, pat
+
+
+def cpu_reference_throughput(budget_s: float, threads: int):
+    """Dense-masked fp32 CPU path on a bounded sample of the same workload.
+
+    Runs whole heads of the three families (B=2, H=16, T=8192) round-robin until ``budget_s``
+    elapsed (at least one head per family); returns live-block TFLOP/s of the sampled heads.
+    """
+    from oracle.bsattn_oracle import attn_dense_masked
+    from usagi_b200 import patterns as P
+    torch.set_num_threads(threads)
+    pats = {f: P.family_pattern(f, B_PER_RANK, H, T) for f in FAMILIES}
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(1, 1, T, D, generator=g)
+    k = torch.randn(1, 1, T, D, generator=g)
+    v = torch.randn(1, 1, T, D, generator=g)
+    flops, n_heads, t_used, per_fam = 0, 0, 0.0, {f: 0 for f in FAMILIES}
+    t_start = time.perf_counter()
+    i = 0
+    while True:
+        fam = FAMILIES[i % len(FAMILIES)]
+        bh = (i // 3) % (B_PER_RANK * H)
+        pat = pats[fam]
+        rp = pat.row_ptr.reshape(-1, T // 128 + 1)[bh:bh + 1].reshape(1, 1, -1)
+        ci = pat.col_idx.reshape(B_PER_RANK * H, -1)[bh:bh + 1].reshape(1, 1, -1)
+        t0 = time.perf_counter()
+        attn_dense_masked(q, k, v, rp, ci)
+        t_used += time.perf_counter() - t0
+        n = rp.reshape(-1).to(torch.int64)
+        lens = n[1:] - n[:-1]
+        flops += int(((lens - 1).clamp(min=0) + 1).sum()) * 4 * 128 ** 3
+        n_heads += 1
+        per_fam[fam] += 1
+        i += 1
+        if i >= len(FAMILIES) and time.perf_counter() - t_start >= budget_s:
+            break
+    tflops = flops / t_used / 1e12
+    return {
+        "value": tflops,
+        "unit": "TFLOP/s",
+        "cores": threads,
+        "kind": "port",
+        "sample": (f"dense-masked fp32 torch CPU path (oracle/bsattn_oracle.attn_dense_masked) on "
+                   f"{n_heads} whole heads (T=8192) of the 3 families ({per_fam}); "
+                   f"{t_used:.1f}s; live-block FLOPs of the sampled heads / CPU time"),
+        "ms_per_head": 1e3 * t_used / n_heads,
+    }
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return 0
+    threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+    per_step = []
+    base = None
+    # keep the whole --steps/--warmup run within a few minutes of CPU time
+    budget = min(args.ref_budget, 150.0 / (args.warmup + args.steps))
+    for s in range(args.warmup + args.steps):
+        r = cpu_reference_throughput(budget_s=budget if s >= args.warmup else 0.0, threads=threads)
+        if s >= args.warmup:
+            per_step.append(r)
+        base = r
+    vals = [r["value"] for r in per_step]
+    v = statistics.median(vals)
+    flops_step = sum(_pattern_flops(f) for f in FAMILIES)
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": v,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": flops_step / (v * 1e12) * 1e3,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f32",
+        "data": "synthetic (seeded N(0,1))",
+        "config": {"workload": "3 families (window8, prefix4+window4, retrieval8) B=2,H=16,T=8192,D=128",
+                   "parallelism": "host cores, rank 0 only"},
+        "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": base["cores"], "kind": "port",
+                         "sample": base["sample"]},
+        "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+_FLOPS_CACHE = {}
+
+
+def _pattern_flops(fam):
+    from usagi_b200 import patterns as P
+    if fam not in _FLOPS_CACHE:
+        _FLOPS_CACHE[fam] = P.family_pattern(fam, B_PER_RANK, H, T).live_blocks() * 4 * 128 ** 3
+    return _FLOPS_CACHE[fam]
+
+
+def measure_e2e(ub, inputs, outs, lses, flops_step, device, world, args):
+    """Same metric through the public API with host buffers: per step and family, H2D of
+    q/k/v/row_ptr/col_idx from pinned memory, the call, D2H of o and lse -- all timed."""
+    import torch.distributed as dist
+    host_in, host_out = {}, {}
+    for f in FAMILIES:
+        q, k, v, rp, ci = inputs[f]
+        host_in[f] = [t.cpu().pin_memory() for t in (q, k, v)] + [rp.cpu().pin_memory(),
+                                                                  ci.cpu().pin_memory()]
+        host_out[f] = (torch.empty(outs[f].shape, dtype=torch.float16).pin_memory(),
+                       torch.empty(lses[f].shape, dtype=torch.float32).pin_memory())
+    h2d = sum(t.numel() * t.element_size() for f in FAMILIES for t in host_in[f])
+    d2h = sum(t.numel() * t.element_size() for f in FAMILIES for t in host_out[f])
+
+    def e2e_step():
+        for f in FAMILIES:
+            hq, hk, hv, hrp, hci = host_in[f]
+            dq, dk, dv = (hq.to(device, non_blocking=True), hk.to(device, non_blocking=True),
+                          hv.to(device, non_blocking=True))
+            drp, dci = hrp.to(device, non_blocking=True), hci.to(device, non_blocking=True)
+            o, lse = ub.block_sparse_attn_fwd(dq, dk, dv, drp, dci, None)
+            host_out[f][0].copy_(o, non_blocking=True)
+            host_out[f][1].copy_(lse, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    t_e2e = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t_e2e, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t_e2e.item())
+    e2e_value = world * flops_step / (e2e_ms * 1e-3) / 1e12
+    return {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
+            "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "path": "usagi_b200.block_sparse_attn_fwd from pinned host buffers, H2D+call+D2H"}
+
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--cpu-budget", type=float, default=12.0,
+                    help="seconds of CPU work for the cpu_baseline sample")
+    ap.add_argument("--ref-budget", type=float, default=4.0,
+                    help="seconds of CPU work per reference-arm step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-gather", action="store_true")
+    ap.add_argument("--family", choices=FAMILIES, default=None,
+                    help="run one family only (profiling); the JSON line then covers that family")
+    ap.add_argument("--quick", action="store_true",
+                    help="device-timed region only: no e2e, cpu_baseline or gather (profiling)")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.family:
+        FAMILIES[:] = [args.family]
+    if args.quick:
+        args.no_cpu_baseline = True
+        args.no_gather = True
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import datetime
+    import torch.distributed as dist
+    import usagi_b200 as ub
+    from usagi_b200 import shard
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+    ub.setup(device=str(device))
+
+    peaks = load_peaks()
+    # Per-rank inputs resident in HBM; CSR metadata on device.
+    inputs = {}
+    for fam in FAMILIES:
+        q, k, v, pat = make_inputs(device, rank, fam)
+        inputs[fam] = (q, k, v, pat.row_ptr.to(device), pat.col_idx.to(device))
+    flops = {f: _pattern_flops(f) for f in FAMILIES}
+    flops_step = sum(flops.values())
+    outs = {f: torch.empty((B_PER_RANK, H, T, D), device=device, dtype=torch.float16)
+            for f in FAMILIES}
+    lses = {f: torch.empty((B_PER_RANK, H, T), device=device, dtype=torch.float32)
+            for f in FAMILIES}
+    flush = torch.empty(512 * 1024 * 1024 // 4, device=device, dtype=torch.float32)
+
+    def call(f):
+        q, k, v, rp, ci = inputs[f]
+        ub.block_sparse_attn_fwd(q, k, v, rp, ci, None, out=outs[f], lse_out=lses[f])
+
+    for _ in range(args.warmup):
+        for f in FAMILIES:
+            flush.zero_()
+            call(f)
+    torch.cuda.synchronize()
+    ub.check_errors(device)
+
+    # ---------------- device-timed region: K steps, L2 flushed before every call
+    n_calls = args.steps * len(FAMILIES)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(n_calls)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        i = 0
+        for _ in range(args.steps):
+            for f in FAMILIES:
+                flush.zero_()
+                ev[i][0].record()
+                call(f)
+                ev[i][1].record()
+                i += 1
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ub.check_errors(device)
+    per_call = [a.elapsed_time(b) for a, b in ev]
+    fam_ms = {f: statistics.median(per_call[j::len(FAMILIES)]) for j, f in enumerate(FAMILIES)}
+    total_ms = sum(per_call)
+    t_kernel = torch.tensor([total_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t_kernel, op=dist.ReduceOp.MAX)
+    total_ms = float(t_kernel.item())
+    ms_per_step = total_ms / args.steps
+    value = world * flops_step / (ms_per_step * 1e-3) / 1e12
+    geo_ms = math.exp(sum(math.log(fam_ms[f]) for f in FAMILIES) / len(FAMILIES))
+    achieved = flops_step / (ms_per_step * 1e-3) / 1e12  # per launch-set on this GPU
+
+    # ---------------- end-to-end through the public API with pinned host buffers
+    e2e = None
+    if not args.quick:
+        e2e = measure_e2e(ub, inputs, outs, lses, flops_step, device, world, args)
+
+    # ---------------- optional gather of o to rank 0 (outside the data path)
+    gather_ms = None
+    if world > 1 and not args.no_gather:
+        gather_ms = shard.timed_gather_to_root(outs[FAMILIES[0]], world, rank, device)
+
+    clocks = clk.summary()
+    line = {
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms_per_step,
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) fp16, CSR patterns generated per family)",
+        "config": {
+            "workload": "3 families (window8, prefix4+window4, retrieval8) B=2,H=16,T=8192,D=128 "
+                        "per GPU; one step = one call per family",
+            "global_batch": B_PER_RANK * world, "heads": H, "seq_len": T, "head_dim": D,
+            "parallelism": f"head-sharded x{world} (batch entries split across ranks, no collective)",
+            "l2": "flushed (512 MB write) before every timed call",
+        },
+        "ms_per_call": fam_ms,
+        "ms_per_call_geomean": geo_ms,
+        "tflops_per_call": {f: flops[f] / (fam_ms[f] * 1e-3) / 1e12 for f in FAMILIES},
+        "gpu_launches": n_calls,
+        "e2e": e2e,
+        "clocks": clocks,
+    }
+    traffic = load_traffic()
+    line["roofline"] = {
+        "bound": "tensor",
+        "kernel": "bsattn_fwd_kernel",
+        "achieved": achieved,
+        "peak": peaks["bf16_tflops"],
+        "peak_source": peaks["source"] + " bf16 dense burst (fp16 runs at the same rate)",
+        "unit": "TFLOP/s",
+        "frac": achieved / peaks["bf16_tflops"],
+        "algorithmic": "live tiles x 4*128^3 FLOP (QK^T + PV, full 128x128 tiles) per launch",
+        "traffic": float(traffic["traffic_bytes_per_launch"]) if traffic and
+        "traffic_bytes_per_launch" in traffic else None,
+        "traffic_note": traffic.get("note") if traffic else None,
+    }
+    if gather_ms is not None:
+        line["gather_ms"] = gather_ms
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
+        line["cpu_baseline"] = cpu_reference_throughput(args.cpu_budget, threads)
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

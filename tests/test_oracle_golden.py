@@ -1,0 +1,115 @@
+"""Pin the CPU oracle against the reference's own outputs (tests/golden, CPU only).
+
+The fixtures hold o (bf16) and lse of the reference Triton kernels (v4 == v7) run under the
+Triton interpreter, whose fp32 -> bf16 store truncates toward zero.  So:
+  * the literal transcription (fp16-rounded P, exp2, running max) truncated to bf16 must
+    reproduce the fixture bit-for-bit on nearly every element and within one bf16 ulp everywhere;
+  * the exact fp32 restatements (blockwise and dense-masked) must sit within one bf16 ulp plus
+    the reference's fp16-P rounding (<= 2e-3) of the fixture;
+  * lse must agree to fp32 precision.
+"""
+import os
+import sys
+
+import numpy as np
+import pytest
+import torch
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "golden"))
+import cases  # noqa: E402
+
+from oracle.bsattn_oracle import (attn_blockwise, attn_dense_masked,  # noqa: E402
+                                  attn_online_literal)
+
+
+def load(name):
+    d = np.load(os.path.join(HERE, "golden", f"{name}.npz"))
+    o = torch.from_numpy(d["o_bf16_bits"]).view(torch.bfloat16).float()
+    return o, torch.from_numpy(d["lse"]), d
+
+
+def trunc_bf16(x: torch.Tensor) -> torch.Tensor:
+    return (x.contiguous().view(torch.int32) & -65536).view(torch.float32)
+
+
+def ulp_bf16(x: torch.Tensor) -> torch.Tensor:
+    ax = x.abs().clamp(min=2.0 ** -126)
+    return torch.exp2(torch.floor(torch.log2(ax)) - 7)
+
+
+@pytest.mark.parametrize("name", cases.CASES)
+def test_inputs_regenerate(name):
+    c = cases.case(name)
+    _, _, d = load(name)
+    for t in "qkv":
+        assert cases.checksum(c[t]) == pytest.approx(float(d[f"{t}_sum"]), rel=0, abs=1e-6), t
+
+
+@pytest.mark.parametrize("name", cases.CASES)
+def test_literal_matches_reference_bits(name):
+    c = cases.case(name)
+    go, gl, _ = load(name)
+    o, lse = attn_online_literal(c["q"], c["k"], c["v"], c["row_ptr"], c["col_idx"], c["seq_lens"])
+    ot = trunc_bf16(o)
+    exact = (ot == go).float().mean().item()
+    assert exact >= 0.99, exact
+    assert ((ot - go).abs() <= ulp_bf16(go) * 1.0001).all()
+    fin = torch.isfinite(gl)
+    assert torch.equal(fin, torch.isfinite(lse))
+    assert (lse[fin] - gl[fin]).abs().max().item() <= 1e-5
+    assert (gl[~fin] == float("-inf")).all()
+
+
+@pytest.mark.parametrize("name", cases.CASES)
+@pytest.mark.parametrize("fn", [attn_blockwise, attn_dense_masked])
+def test_exact_oracles_match_reference(name, fn):
+    c = cases.case(name)
+    go, gl, _ = load(name)
+    o, lse = fn(c["q"], c["k"], c["v"], c["row_ptr"], c["col_idx"], c["seq_lens"])
+    err = (o - go).abs()
+    assert (err <= ulp_bf16(go) + 2e-3).all(), err.max().item()
+    assert err.mean().item() <= 1e-3
+    fin = torch.isfinite(gl)
+    assert torch.equal(fin, torch.isfinite(lse))
+    assert (lse[fin] - gl[fin]).abs().max().item() <= 1e-4
+
+
+def _v1_semantics(q, k, v, row_ptr, col_idx, seq_lens):
+    """A deliberately wrong oracle: treats every CSR entry (including the last) as a block and
+    masks causally only when kb == qb -- the unified loop of kernels/v1_baseline.py:372-383."""
+    B, H, T, D = q.shape
+    nqb = T // 128
+    rp = row_ptr.reshape(B * H, nqb + 1)
+    ci = col_idx.reshape(B * H, -1)
+    o = torch.zeros(B * H, T, D)
+    qf, kf, vf = (x.reshape(B * H, T, D).float() for x in (q, k, v))
+    ar = torch.arange(128)
+    for bh in range(B * H):
+        for qb in range(nqb):
+            blocks = [int(x) for x in ci[bh, int(rp[bh, qb]):int(rp[bh, qb + 1])]]
+            if not blocks:
+                continue
+            idx = torch.cat([torch.arange(b * 128, b * 128 + 128) for b in blocks])
+            s = qf[bh, qb * 128:qb * 128 + 128] @ kf[bh, idx].T / 128 ** 0.5
+            for i, b in enumerate(blocks):
+                if b == qb:
+                    s[:, i * 128:(i + 1) * 128].masked_fill_(ar[None, :] > ar[:, None], float("-inf"))
+            o[bh, qb * 128:qb * 128 + 128] = torch.softmax(s, 1) @ vf[bh, idx]
+    return o.reshape(B, H, T, D)
+
+
+def test_golden_discriminates_semantics():
+    """A planted mistake in the oracle (v1's CSR semantics) must fail the irregular fixture."""
+    c = cases.case("irregular")
+    go, _, _ = load("irregular")
+    o = _v1_semantics(c["q"], c["k"], c["v"], c["row_ptr"], c["col_idx"], c["seq_lens"])
+    assert (o - go).abs().max().item() > 0.05
+
+
+def test_golden_discriminates_scale():
+    """A planted mistake (softmax scale 1/128 instead of 1/sqrt(128)) must fail the fixtures."""
+    c = cases.case("cfg0_window4")
+    go, gl, _ = load("cfg0_window4")
+    o, lse = attn_blockwise(c["q"], c["k"], c["v"], c["row_ptr"], c["col_idx"], None, scale=1 / 128)
+    assert (o - go).abs().max().item() > 0.05

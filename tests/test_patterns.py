@@ -1,0 +1,63 @@
+"""CSR family generators: live-block counts, row structure, determinism (CPU)."""
+import torch
+
+from usagi_b200 import patterns as P
+
+
+def rows_of(pat, bh):
+    rp = pat.row_ptr.reshape(-1, pat.nqb + 1)[bh]
+    ci = pat.col_idx.reshape(-1, pat.col_idx.shape[-1])[bh]
+    return [ci[int(rp[i]):int(rp[i + 1])].tolist() for i in range(pat.nqb)]
+
+
+def test_live_block_counts_match_benchmark_configs():
+    assert P.family_pattern("window8", 2, 16, 8192).live_blocks() == 15488
+    assert P.family_pattern("prefix4+window4", 2, 16, 8192).live_blocks() == 15488
+    assert P.family_pattern("retrieval8", 2, 16, 8192).live_blocks() == 19040
+    assert P.window_pattern(1, 2, 1024, 4).live_blocks() == 52
+
+
+def test_mixed_scaling_pattern_count():
+    # B=4, H=32, T=32768: window16 / prefix8+window8 / retrieval(2+16) by bh % 3, seed 1.
+    assert P.mixed_pattern(4, 32, 32768).live_blocks() == 529046
+
+
+def test_rows_sorted_and_end_with_diagonal():
+    for name in ["window8", "prefix4+window4", "retrieval8"]:
+        pat = P.family_pattern(name, 1, 3, 4096)
+        for bh in range(3):
+            for i, r in enumerate(rows_of(pat, bh)):
+                assert r == sorted(set(r)), (name, bh, i)
+                assert r[-1] == i
+                assert all(0 <= c <= i for c in r)
+
+
+def test_retrieval_row_contents():
+    pat = P.retrieval_pattern(1, 1, 64 * 128, 8, seed=1)
+    rows = rows_of(pat, 0)
+    assert rows[0] == [0] and rows[1] == [0, 1]
+    for i in range(2, 64):
+        r = rows[i]
+        assert i in r and i - 1 in r
+        assert len(r) == 2 + min(8, i - 1)
+
+
+def test_retrieval_deterministic_and_per_head():
+    a = P.retrieval_pattern(2, 2, 2048, 8, seed=1)
+    b = P.retrieval_pattern(2, 2, 2048, 8, seed=1)
+    assert torch.equal(a.row_ptr, b.row_ptr) and torch.equal(a.col_idx, b.col_idx)
+    assert not torch.equal(a.col_idx[0, 0], a.col_idx[0, 1])
+
+
+def test_shared_equals_materialized():
+    s = P.window_pattern(2, 3, 2048, 8, shared=True)
+    m = P.window_pattern(2, 3, 2048, 8, shared=False)
+    assert s.row_ptr.stride(0) == 0 and s.row_ptr.stride(1) == 0
+    assert torch.equal(s.row_ptr.contiguous(), m.row_ptr)
+    assert torch.equal(s.col_idx.contiguous()[..., : m.col_idx.shape[-1]], m.col_idx)
+
+
+def test_prefix_window_rows():
+    r = P.prefix_window_rows(10, 4, 4)
+    assert r[0] == [0] and r[3] == [0, 1, 2, 3] and r[4] == [0, 1, 2, 3, 4]
+    assert r[9] == [0, 1, 2, 3, 6, 7, 8, 9]

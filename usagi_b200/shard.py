@@ -1,0 +1,94 @@
+"""Head sharding across the GPUs of one node (one process per GPU).
+
+Every (batch, head) pair of block-sparse attention is independent, so a problem is split by
+flattened head index bh = b*H + h into contiguous, near-equal ranges -- no exchange on the data
+path.  When the caller wants all outputs on one device, ``gather_to_root`` collects the o shards
+on rank 0 with one NCCL (or gloo, on CPU) collective.  The reference has no multi-GPU code; this
+is the partitioning its (B*H, T/128) grid (kernels/v4_leaderboard_0740ms.py:166-167) implies.
+"""
+from __future__ import annotations
+
+from typing import Optional, Tuple
+
+import torch
+
+__all__ = ["shard_range", "shard_problem", "gather_to_root", "timed_gather_to_root"]
+
+
+def shard_range(n: int, world: int, rank: int) -> Tuple[int, int]:
+    """Contiguous [start, end) slice of n units for `rank`; sizes differ by at most one."""
+    if world < 1 or not (0 <= rank < world):
+        raise ValueError(f"bad world/rank {world}/{rank}")
+    base, rem = divmod(n, world)
+    start = rank * base + min(rank, rem)
+    return start, start + base + (1 if rank < rem else 0)
+
+
+def shard_problem(q, k, v, row_ptr, col_idx, seq_lens: Optional[torch.Tensor], world: int,
+                  rank: int):
+    """Slice one rank's heads out of a [B, H, T, D] problem.
+
+    Returns (q, k, v, row_ptr, col_idx, seq_lens, (start, end)) where the tensors are shaped as a
+    problem with B' = end - start heads of one "batch entry" each (H' = 1), so per-head seq_lens
+    follow the heads they belong to.
+    """
+    B, H, T, D = q.shape
+    start, end = shard_range(B * H, world, rank)
+    n = end - start
+
+    def heads(t):
+        return t.reshape(B * H, *t.shape[2:])[start:end].reshape(n, 1, *t.shape[2:])
+
+    def meta(t):
+        if t.dim() == 1:  # one shared row for every head
+            return t
+        if t.dim() == 2:
+            return t[start:end].reshape(n, 1, -1)
+        return t.reshape(B * H, -1)[start:end].reshape(n, 1, -1)
+
+    sl = None
+    if seq_lens is not None:
+        sl = seq_lens.reshape(B).repeat_interleave(H)[start:end].contiguous()
+    return heads(q), heads(k), heads(v), meta(row_ptr), meta(col_idx), sl, (start, end)
+
+
+def gather_to_root(o_shard: torch.Tensor, total_heads: int, world: int, rank: int,
+                   group=None) -> Optional[torch.Tensor]:
+    """Gather per-rank o shards ([n_r, ...] heads) into [total_heads, ...] on rank 0.
+
+    Shards are padded to the largest shard so the collective sees equal sizes. Returns the
+    gathered tensor on rank 0 and None elsewhere.  Every rank must call this.
+    """
+    import torch.distributed as dist
+    per = -(-total_heads // world)
+    flat = o_shard.reshape(o_shard.shape[0], -1)
+    if flat.shape[0] < per:
+        pad = torch.zeros((per - flat.shape[0], flat.shape[1]), dtype=flat.dtype, device=flat.device)
+        flat = torch.cat([flat, pad], 0)
+    flat = flat.contiguous()
+    out_list = [torch.empty_like(flat) for _ in range(world)] if rank == 0 else None
+    dist.gather(flat, gather_list=out_list, dst=0, group=group)
+    if rank != 0:
+        return None
+    parts = []
+    for r in range(world):
+        s, e = shard_range(total_heads, world, r)
+        parts.append(out_list[r][: e - s])
+    return torch.cat(parts, 0).reshape(total_heads, *o_shard.shape[1:])
+
+
+def timed_gather_to_root(o_shard: torch.Tensor, world: int, rank: int, device) -> float:
+    """Device time (ms, max over ranks) of gathering every rank's o shard onto rank 0."""
+    import torch.distributed as dist
+    total = o_shard.shape[0] * world
+    gather_to_root(o_shard, total, world, rank)  # warm-up (communicator setup)
+    torch.cuda.synchronize(device)
+    dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    gather_to_root(o_shard, total, world, rank)
+    e1.record()
+    torch.cuda.synchronize(device)
+    t = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
