@@ -14,11 +14,17 @@
 //   * Persistent CTAs, one per SM, each running two independent query-tile "slots".  Items
 //     (bh, qb) are dealt round-robin in order of decreasing qb, so the longest causal rows go
 //     first and every CTA sees the same mix.
-//   * Warp roles (320 threads):
+//   * Warp roles (384 threads).  setmaxnreg gives the softmax warpgroups 208 registers and the
+//     control warpgroup 88; every device function is inlined, because a called function has
+//     one register allocation and cannot serve both budgets.
 //       warps 0-3  softmax + epilogue for slot 0   (thread t owns query row t of the tile)
 //       warps 4-7  softmax + epilogue for slot 1
 //       warp  8    TMA producer: Q tiles per item, K/V tiles named by col_idx into a ring
-//       warp  9    tcgen05 MMA issuer (single thread) and TMEM owner
+//       warp  9    tcgen05 MMA issuer and TMEM owner
+//     The producer and MMA warps run their schedules with all 32 lanes so that addresses and
+//     descriptors are warp-uniform (the form TMA and tcgen05.mma take their operands in); only
+//     lane 0 issues the copies, MMAs and commits.
+//       warps 10-11 idle (they complete warpgroup 2 for the register re-allocation)
 //   * Tensor memory (512 columns x 128 lanes x 32 bit):
 //       slot s: S = Q K^T (fp32) at columns [256 s, 256 s + 128), O (fp32) at [256 s + 128, 256 s + 256)
 //       P (fp16, two per column) overwrites the first 64 columns of S and is the A operand of the
@@ -53,11 +59,20 @@ constexpr int kHd = 128;                   // head dimension
 constexpr int kStages = 4;                 // K/V ring depth
 constexpr int kTileBytes = kBlk * kHd * 2; // 32 KB fp16 tile
 constexpr int kBoxBytes = kTileBytes / 2;  // one TMA box: 128 rows x 64 columns, 128B swizzle
-constexpr int kThreads = 320;
+constexpr int kThreads = 384;            // 3 warpgroups
 constexpr int kLoadWarp = 8;
 constexpr int kMmaWarp = 9;
 constexpr uint32_t kTmemCols = 512;
 constexpr float kRescaleLog2 = 8.0f;
+constexpr int kPolyEvery = 4;              // every 4th pair of exponentials runs on the FMA pipe
+// setmaxnreg budgets.  The increase draws only on the registers the block was launched with
+// (384 threads x 168 = 64512), so per SMSP lane-slot (two softmax warps + one control warp)
+// 2 * kSoftmaxRegs + kControlRegs must not exceed 3 * kLaunchRegs, or the increase never returns.
+constexpr uint32_t kLaunchRegs = 168;      // ptxas allocation for __launch_bounds__(384, 1)
+constexpr uint32_t kSoftmaxRegs = 208;
+constexpr uint32_t kControlRegs = 88;
+static_assert(2 * kSoftmaxRegs + kControlRegs <= 3 * kLaunchRegs, "register split exceeds launch");
+static_assert(kLaunchRegs * kThreads <= 65536, "launch register total");
 constexpr int kWsInts = 64;                // workspace: int32[64]
 constexpr uint32_t kIdescQK = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescPV = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/true);
@@ -70,7 +85,8 @@ struct alignas(1024) SharedStorage {
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
   uint64_t s_full[2];
-  uint64_t p_ready[2];
+  uint64_t p_lo[2];   // P columns for keys 0..63 stored (and O rescaled if needed)
+  uint64_t p_hi[2];   // P columns for keys 64..127 stored
   uint64_t o_full[2];
   uint64_t drain;
   uint32_t tmem_base;
@@ -151,7 +167,7 @@ __device__ __forceinline__ void raise_error(const FwdParams& p, int code) {
 
 // Bounded wait: true when the phase completed; false when this CTA aborted or the wait ran
 // past p.timeout_ns (then it raises the abort flag and the timeout error).
-__device__ __noinline__ bool wait_slow(uint32_t bar, uint32_t parity, SharedStorage& sh,
+__device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, SharedStorage& sh,
                                        const FwdParams& p) {
   const uint64_t t0 = ptx::globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
@@ -174,7 +190,7 @@ __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, SharedSt
 }
 
 // Drain wait used during teardown: ignores the abort flag, still bounded in time.
-__device__ __noinline__ void wait_drain(uint32_t bar, uint32_t parity, const FwdParams& p) {
+__device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity, const FwdParams& p) {
   const uint64_t t0 = ptx::globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (ptx::mbar_try_wait(bar, parity)) return;
@@ -185,36 +201,48 @@ __device__ __noinline__ void wait_drain(uint32_t bar, uint32_t parity, const Fwd
   }
 }
 
+// Bounded wait executed by a whole warp; the result is the same on every lane.
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, SharedStorage& sh,
+                                          const FwdParams& p) {
+  return __all_sync(0xffffffffu, wait_bar(bar, parity, sh, p));
+}
+
 // ------------------------------------------------------------------------------------------
-// Producer (one thread): mirrors the MMA issue order exactly -- S(first) of slot 0 and 1, then
-// per slot "V(j), K(j+1)" -- so the ring holds tiles in the order the MMAs consume them.
+// Producer warp: mirrors the MMA issue order exactly -- S(first) of slot 0 and 1, then per slot
+// "V(j), K(j+1)" -- so the ring holds tiles in the order the MMAs consume them.  The whole warp
+// runs the control flow (so coordinates stay warp-uniform, which is what the TMA instruction
+// consumes); lane 0 alone issues the copies.
 // ------------------------------------------------------------------------------------------
 __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CUtensorMap* tk,
-                              const CUtensorMap* tv, const FwdParams& p) {
+                              const CUtensorMap* tv, const FwdParams& p, bool leader) {
   bool csr_bad = false;
   const uint64_t pol_kv = ptx::policy_evict_last();
   const uint64_t pol_q = ptx::policy_evict_first();
   Stream st[2];
   bool has[2];
   uint32_t qe_phase[2] = {0, 0};
-  int q_issued[2] = {0, 0};
-  uint32_t q_last_parity[2] = {0, 0};
+  uint32_t q_issued = 0, q_last_parity = 0;    // bit s: slot s
   int stage = 0;
   uint32_t kv_phase = 0;
   uint32_t kv_issued = 0;       // bit i: stage i received at least one load
   uint32_t kv_last_parity = 0;  // bit i: phase parity of the last load into stage i
-  const uint32_t q_smem[2] = {ptx::smem_u32(sh.q[0]), ptx::smem_u32(sh.q[1])};
+  const uint32_t q_smem0 = ptx::smem_u32(sh.q[0]);
   const uint32_t kv_smem0 = ptx::smem_u32(sh.kv[0]);
+  const uint32_t kv_full0 = ptx::smem_u32(&sh.kv_full[0]);
+  const uint32_t kv_empty0 = ptx::smem_u32(&sh.kv_empty[0]);
   bool ok = true;
 
   auto load_tile = [&](const CUtensorMap* map, int row) -> bool {
-    const uint32_t empty = ptx::smem_u32(&sh.kv_empty[stage]);
-    const uint32_t full = ptx::smem_u32(&sh.kv_full[stage]);
-    if (!wait_bar(empty, kv_phase ^ 1u, sh, p)) return false;
-    ptx::mbar_expect_tx(full, kTileBytes);
-    const uint32_t dst = kv_smem0 + stage * kTileBytes;
-    ptx::tma_load_2d(dst, map, full, 0, row, pol_kv);
-    ptx::tma_load_2d(dst + kBoxBytes, map, full, 64, row, pol_kv);
+    const uint32_t empty = kv_empty0 + stage * 8;
+    const uint32_t full = kv_full0 + stage * 8;
+    if (!wait_warp(empty, kv_phase ^ 1u, sh, p)) return false;
+    if (leader) {
+      const uint32_t dst = kv_smem0 + stage * kTileBytes;
+      ptx::mbar_expect_tx(full, kTileBytes);
+      ptx::tma_load_2d(dst, map, full, 0, row, pol_kv);
+      ptx::tma_load_2d(dst + kBoxBytes, map, full, 64, row, pol_kv);
+    }
+    __syncwarp();
     kv_issued |= 1u << stage;
     kv_last_parity = (kv_last_parity & ~(1u << stage)) | (kv_phase << stage);
     if (++stage == kStages) stage = 0, kv_phase ^= 1u;
@@ -226,13 +254,17 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
     if (x.j == 0) {
       const uint32_t empty = ptx::smem_u32(&sh.q_empty[s]);
       const uint32_t full = ptx::smem_u32(&sh.q_full[s]);
-      if (!wait_bar(empty, qe_phase[s] ^ 1u, sh, p)) return false;
-      ptx::mbar_expect_tx(full, kTileBytes);
-      const int row = head_row0 + x.it.qb * kBlk;
-      ptx::tma_load_2d(q_smem[s], tq, full, 0, row, pol_q);
-      ptx::tma_load_2d(q_smem[s] + kBoxBytes, tq, full, 64, row, pol_q);
-      q_issued[s] = 1;
-      q_last_parity[s] = qe_phase[s];
+      if (!wait_warp(empty, qe_phase[s] ^ 1u, sh, p)) return false;
+      if (leader) {
+        const uint32_t dst = q_smem0 + s * kTileBytes;
+        const int row = head_row0 + x.it.qb * kBlk;
+        ptx::mbar_expect_tx(full, kTileBytes);
+        ptx::tma_load_2d(dst, tq, full, 0, row, pol_q);
+        ptx::tma_load_2d(dst + kBoxBytes, tq, full, 64, row, pol_q);
+      }
+      __syncwarp();
+      q_issued |= 1u << s;
+      q_last_parity = (q_last_parity & ~(1u << s)) | (qe_phase[s] << s);
       qe_phase[s] ^= 1u;
     }
     int kb = x.it.qb;  // diagonal
@@ -270,70 +302,93 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
       }
     }
   }
-  if (csr_bad) raise_error(p, BSATTN_E_CSR);
+  if (csr_bad && leader) raise_error(p, BSATTN_E_CSR);
   if (!ok) {
     // Aborted: make sure no TMA write is still landing in shared memory before the CTA exits.
     for (int i = 0; i < kStages; ++i)
-      if ((kv_issued >> i) & 1u) wait_drain(ptx::smem_u32(&sh.kv_full[i]), (kv_last_parity >> i) & 1u, p);
+      if ((kv_issued >> i) & 1u) wait_drain(kv_full0 + i * 8, (kv_last_parity >> i) & 1u, p);
     for (int s = 0; s < 2; ++s)
-      if (q_issued[s]) wait_drain(ptx::smem_u32(&sh.q_full[s]), q_last_parity[s], p);
+      if ((q_issued >> s) & 1u)
+        wait_drain(ptx::smem_u32(&sh.q_full[s]), (q_last_parity >> s) & 1u, p);
   }
 }
 
 // ------------------------------------------------------------------------------------------
-// MMA issuer (one thread).
+// MMA warp: the whole warp runs the schedule and builds the descriptors (warp-uniform values);
+// lane 0 issues every tcgen05.mma and tcgen05.commit, so one thread owns all MMA completions.
+// Descriptors are formed once and advanced by adding (byte offset >> 4) to the start-address
+// field, which never carries out of its 14 bits inside the 227 KB of shared memory.
 // ------------------------------------------------------------------------------------------
-__device__ void mma_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem) {
+__device__ void mma_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem, bool leader) {
   Stream st[2];
   bool has[2];
   uint32_t qf_phase[2] = {0, 0};
   uint32_t pr_phase[2] = {0, 0};
   int stage = 0;
   uint32_t kv_phase = 0;
-  const uint32_t q_smem[2] = {ptx::smem_u32(sh.q[0]), ptx::smem_u32(sh.q[1])};
-  const uint32_t kv_smem0 = ptx::smem_u32(sh.kv[0]);
+  const uint64_t q_desc0 = ptx::sdesc_sw128(ptx::smem_u32(sh.q[0]), 16, 1024);
+  const uint64_t k_desc0 = ptx::sdesc_sw128(ptx::smem_u32(sh.kv[0]), 16, 1024);
+  const uint64_t v_desc0 = ptx::sdesc_sw128(ptx::smem_u32(sh.kv[0]), kBoxBytes, 1024);
+  const uint32_t kv_full0 = ptx::smem_u32(&sh.kv_full[0]);
+  const uint32_t kv_empty0 = ptx::smem_u32(&sh.kv_empty[0]);
   bool ok = true;
 
   auto issue_S = [&](int s) -> bool {
     Stream& x = st[s];
     if (x.j == 0) {
-      if (!wait_bar(ptx::smem_u32(&sh.q_full[s]), qf_phase[s], sh, p)) return false;
+      if (!wait_warp(ptx::smem_u32(&sh.q_full[s]), qf_phase[s], sh, p)) return false;
       qf_phase[s] ^= 1u;
     }
-    if (!wait_bar(ptx::smem_u32(&sh.kv_full[stage]), kv_phase, sh, p)) return false;
+    if (!wait_warp(kv_full0 + stage * 8, kv_phase, sh, p)) return false;
     ptx::tc_fence_after();
-    const uint32_t kaddr = kv_smem0 + stage * kTileBytes;
+    const uint64_t qd = q_desc0 + static_cast<uint32_t>((s * kTileBytes) >> 4);
+    const uint64_t kd = k_desc0 + static_cast<uint32_t>((stage * kTileBytes) >> 4);
     const uint32_t d = tmem + s * 256;
+    if (leader) {
 #pragma unroll
-    for (int kk = 0; kk < kHd / 16; ++kk) {
-      const uint32_t off = (kk >> 2) * kBoxBytes + (kk & 3) * 32;
-      ptx::mma_ss(d, ptx::sdesc_sw128(q_smem[s] + off, 16, 1024),
-                  ptx::sdesc_sw128(kaddr + off, 16, 1024), kIdescQK, kk > 0 ? 1u : 0u);
+      for (int kk = 0; kk < kHd / 16; ++kk) {
+        const uint32_t off = ((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4;
+        ptx::mma_ss(d, qd + off, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
+      }
+      ptx::tc_commit(kv_empty0 + stage * 8);
+      ptx::tc_commit(ptx::smem_u32(&sh.s_full[s]));
+      if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.q_empty[s]));
     }
-    ptx::tc_commit(ptx::smem_u32(&sh.kv_empty[stage]));
-    ptx::tc_commit(ptx::smem_u32(&sh.s_full[s]));
-    if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.q_empty[s]));
+    __syncwarp();
     if (++stage == kStages) stage = 0, kv_phase ^= 1u;
     return true;
   };
   auto issue_PV = [&](int s) -> bool {
     Stream& x = st[s];
-    if (!wait_bar(ptx::smem_u32(&sh.p_ready[s]), pr_phase[s], sh, p)) return false;
-    pr_phase[s] ^= 1u;
-    if (!wait_bar(ptx::smem_u32(&sh.kv_full[stage]), kv_phase, sh, p)) return false;
-    ptx::tc_fence_after();
-    const uint32_t vaddr = kv_smem0 + stage * kTileBytes;
+    if (!wait_warp(kv_full0 + stage * 8, kv_phase, sh, p)) return false;
+    const uint64_t vd = v_desc0 + static_cast<uint32_t>((stage * kTileBytes) >> 4);
     const uint32_t d = tmem + s * 256 + 128;
     const uint32_t a = tmem + s * 256;
+    // P arrives in two halves (keys 0..63, 64..127); the first four K-steps start as soon as the
+    // first half is in tensor memory.
 #pragma unroll
-    for (int kk = 0; kk < kBlk / 16; ++kk) {
-      // V is [key][d] with d contiguous: MN-major B operand.  One K step = 16 keys = two
-      // 8-row swizzle atoms (2 KB); the second 64-column half of d sits one TMA box later.
-      ptx::mma_ts(d, a + kk * 8, ptx::sdesc_sw128(vaddr + kk * 2048, kBoxBytes, 1024), kIdescPV,
-                  (x.j > 0 || kk > 0) ? 1u : 0u);
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t bar = ptx::smem_u32(half == 0 ? &sh.p_lo[s] : &sh.p_hi[s]);
+      if (!wait_warp(bar, pr_phase[s], sh, p)) return false;
+      ptx::tc_fence_after();
+      if (leader) {
+#pragma unroll
+        for (int k4 = 0; k4 < 4; ++k4) {
+          const int kk = half * 4 + k4;
+          // V is [key][d] with d contiguous: MN-major B operand.  One K step = 16 keys = two
+          // 8-row swizzle atoms (2 KB); the second 64-column half of d sits one TMA box later.
+          ptx::mma_ts(d, a + kk * 8, vd + static_cast<uint32_t>((kk * 2048) >> 4), kIdescPV,
+                      (x.j > 0 || kk > 0) ? 1u : 0u);
+        }
+      }
+      __syncwarp();
     }
-    ptx::tc_commit(ptx::smem_u32(&sh.kv_empty[stage]));
-    if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.o_full[s]));
+    pr_phase[s] ^= 1u;
+    if (leader) {
+      ptx::tc_commit(kv_empty0 + stage * 8);
+      if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.o_full[s]));
+    }
+    __syncwarp();
     if (++stage == kStages) stage = 0, kv_phase ^= 1u;
     return true;
   };
@@ -394,7 +449,8 @@ __device__ void softmax_role(SharedStorage& sh, const FwdParams& p, int slot, ui
   const uint32_t s_addr = lane_addr + slot * 256;
   const uint32_t o_addr = s_addr + 128;
   const uint32_t s_full = ptx::smem_u32(&sh.s_full[slot]);
-  const uint32_t p_ready = ptx::smem_u32(&sh.p_ready[slot]);
+  const uint32_t p_lo = ptx::smem_u32(&sh.p_lo[slot]);
+  const uint32_t p_hi = ptx::smem_u32(&sh.p_hi[slot]);
   const uint32_t o_full = ptx::smem_u32(&sh.o_full[slot]);
   uint32_t sf_phase = 0, of_phase = 0;
   const float sl2 = p.scale_log2;
@@ -441,19 +497,20 @@ __device__ void softmax_role(SharedStorage& sh, const FwdParams& p, int slot, ui
 #pragma unroll
         for (int c = 0; c < 128; ++c) s[c] = (c < n_keep) ? s[c] : -INFINITY;
       }
-      float mx[8];
+      // Row max of the raw scores (scale > 0 commutes with max), three inputs per instruction.
+      float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
 #pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = s[i];
-#pragma unroll
-      for (int c = 8; c < 128; c += 8) {
-#pragma unroll
-        for (int i = 0; i < 8; ++i) mx[i] = fmaxf(mx[i], s[c + i]);
+      for (int c = 4; c < 124; c += 8) {
+        a0 = ptx::fmax3(a0, s[c + 0], s[c + 1]);
+        a1 = ptx::fmax3(a1, s[c + 2], s[c + 3]);
+        a2 = ptx::fmax3(a2, s[c + 4], s[c + 5]);
+        a3 = ptx::fmax3(a3, s[c + 6], s[c + 7]);
       }
-      const float mblk = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                               fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      const float m_cand = mblk * sl2;
+      a0 = ptx::fmax3(a0, s[124], s[125]);
+      a1 = ptx::fmax3(a1, s[126], s[127]);
+      const float m_cand = ptx::fmax3(a0, a1, fmaxf(a2, a3)) * sl2;
       // Decide the new running max before touching O: P is computed against it, and O is
-      // rescaled after P has been stored (keeps S and the O chunk from being live together).
+      // rescaled before the first half of P is released to the MMA.
       float alpha = 1.0f;
       bool rescale = false;
       if (j == 0) {
@@ -468,44 +525,57 @@ __device__ void softmax_role(SharedStorage& sh, const FwdParams& p, int slot, ui
           m_run = m_new;
         }
       }
-      const float neg_m = -m_run;
-      float sum[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) sum[i] = 0.0f;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        s[c] = ptx::ex2(fmaf(s[c], sl2, neg_m));
-        sum[c & 7] += s[c];
-      }
-      l_run += ((sum[0] + sum[1]) + (sum[2] + sum[3])) + ((sum[4] + sum[5]) + (sum[6] + sum[7]));
+      // p = 2^(s*scale - m) on pairs: one packed FMA per pair, MUFU for most exponentials and
+      // the FMA-pipe polynomial for every kPolyEvery-th pair; the row sum l accumulates the
+      // fp32 p (v4 :99) in packed adds; P is stored as fp16 pairs (v4 :103).
+      const uint64_t sc2 = ptx::pack2(sl2, sl2);
+      const uint64_t nm2 = ptx::pack2(-m_run, -m_run);
+      uint64_t acc0 = 0, acc1 = 0;
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         uint32_t pk[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
-          __half2 hv = __floats2half2_rn(s[64 * h + 2 * i], s[64 * h + 2 * i + 1]);
+          const int c = 64 * h + 2 * i;
+          const uint64_t x2 = ptx::ffma2(ptx::pack2(s[c], s[c + 1]), sc2, nm2);
+          float x0, x1, p0, p1;
+          ptx::unpack2(x2, x0, x1);
+          if (kPolyEvery > 0 && (i % kPolyEvery) == kPolyEvery - 1) {
+            ptx::exp2_poly_pair(x0, x1, p0, p1);
+          } else {
+            p0 = ptx::ex2(x0);
+            p1 = ptx::ex2(x1);
+          }
+          const uint64_t p2 = ptx::pack2(p0, p1);
+          if (i & 1) acc1 = ptx::fadd2(acc1, p2); else acc0 = ptx::fadd2(acc0, p2);
+          __half2 hv = __floats2half2_rn(p0, p1);
           pk[i] = *reinterpret_cast<uint32_t*>(&hv);
         }
         ptx::tmem_st32(s_addr + 32 * h, pk);
-      }
-      if (rescale) {
-        // O holds the sum through PV(j-1), which completed before S(j) was committed.
+        if (h == 0 && rescale) {
+          // O holds the sum through PV(j-1), which completed before S(j) was committed.
 #pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t orow[32];
-          ptx::tmem_ld32(o_addr + c * 32, orow);
-          ptx::tmem_wait_ld();
+          for (int c = 0; c < 4; ++c) {
+            uint32_t orow[32];
+            ptx::tmem_ld32(o_addr + c * 32, orow);
+            ptx::tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            ptx::reg_fence(orow[i]);
-            orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+            for (int i = 0; i < 32; ++i) {
+              ptx::reg_fence(orow[i]);
+              orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+            }
+            ptx::tmem_st32(o_addr + c * 32, orow);
           }
-          ptx::tmem_st32(o_addr + c * 32, orow);
         }
+        ptx::tmem_wait_st();
+        ptx::tc_fence_before();
+        ptx::mbar_arrive(h == 0 ? p_lo : p_hi);
       }
-      ptx::tmem_wait_st();
-      ptx::tc_fence_before();
-      ptx::mbar_arrive(p_ready);
+      float l0, l1, l2, l3;
+      ptx::unpack2(ptx::fadd2(acc0, acc1), l0, l1);
+      (void)l2;
+      (void)l3;
+      l_run += l0 + l1;
     }
 
     // Epilogue: o = O / l (v4 :126-133), lse = m ln2 + ln l (v4 :134-136).
@@ -550,7 +620,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       ptx::mbar_init(ptx::smem_u32(&sh.q_full[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&sh.q_empty[s]), 1);
       ptx::mbar_init(ptx::smem_u32(&sh.s_full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&sh.p_ready[s]), 128);
+      ptx::mbar_init(ptx::smem_u32(&sh.p_lo[s]), 128);
+      ptx::mbar_init(ptx::smem_u32(&sh.p_hi[s]), 128);
       ptx::mbar_init(ptx::smem_u32(&sh.o_full[s]), 1);
     }
     for (int i = 0; i < kStages; ++i) {
@@ -576,11 +647,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = sh.tmem_base;
 
   if (warp < 8) {
+    ptx::setmaxnreg_inc<kSoftmaxRegs>();
     softmax_role(sh, p, warp >> 2, tmem);
-  } else if (warp == kLoadWarp) {
-    if (lane == 0) producer_role(sh, &tq, &tk, &tv, p);
-  } else if (warp == kMmaWarp) {
-    if (lane == 0) mma_role(sh, p, tmem);
+  } else {
+    ptx::setmaxnreg_dec<kControlRegs>();
+    if (warp == kLoadWarp) {
+      producer_role(sh, &tq, &tk, &tv, p, lane == 0);
+    } else if (warp == kMmaWarp) {
+      mma_role(sh, p, tmem, lane == 0);
+    }
   }
   __syncwarp();
   ptx::tc_fence_before();
@@ -658,6 +733,13 @@ static int device_setup(int* sms_out) {
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
       return BSATTN_E_CUDA;
     if (major != 10) return BSATTN_E_DEVICE;
+    // The warpgroup register split only works if the kernel was built with the register count
+    // it assumes; a smaller launch allocation would make setmaxnreg.inc wait forever.
+    cudaFuncAttributes fa;
+    if (cudaFuncGetAttributes(&fa, bsattn_fwd_kernel) != cudaSuccess) return BSATTN_E_CUDA;
+    if (fa.numRegs < static_cast<int>(kLaunchRegs) ||
+        fa.numRegs * kThreads > 65536)
+      return BSATTN_E_CUDA;
     if (cudaFuncSetAttribute(bsattn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem_bytes())) != cudaSuccess)
       return BSATTN_E_CUDA;

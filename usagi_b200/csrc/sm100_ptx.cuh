@@ -198,11 +198,76 @@ __device__ __forceinline__ void tmem_wait_st() {
 // cannot hoist its uses above that instruction.
 __device__ __forceinline__ void reg_fence(uint32_t& x) { asm volatile("" : "+r"(x)); }
 
+// Warpgroup register re-allocation (all four warps of a warpgroup execute it).
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void setmaxnreg_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
+}
+
+// Three-input maximum (one instruction on sm_100).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// Packed pairs of fp32 in one 64-bit register pair, for the sm_100 f32x2 FMA/ADD instructions.
+__device__ __forceinline__ uint64_t pack2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void unpack2(uint64_t r, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(r));
+}
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t fadd2(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
 // Hardware base-2 exponential (MUFU.EX2), flush-to-zero.
 __device__ __forceinline__ float ex2(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// 2^x for a pair of fp32 values on the FMA pipe instead of MUFU: round x to the nearest
+// integer j with the 1.5*2^23 shifter, evaluate 2^(x-j), x-j in [-0.5, 0.5], with a degree-4
+// polynomial fitted here (least squares in relative error at Chebyshev nodes, refined toward
+// minimax; max relative error 2.7e-6 in fp32 Horner evaluation), then add j to the exponent
+// field.  Inputs are clamped at -126: the polynomial can return slightly less than 1 (exponent
+// field 126), so -126 is the lowest shift that cannot borrow into the sign bit.  Masked (-inf)
+// scores therefore give a value below 1.2e-38, which rounds to 0 in fp16.
+__device__ __forceinline__ void exp2_poly_pair(float x0, float x1, float& y0, float& y1) {
+  x0 = fmaxf(x0, -126.0f);
+  x1 = fmaxf(x1, -126.0f);
+  const uint64_t X = pack2(x0, x1);
+  const uint64_t shifter = pack2(12582912.0f, 12582912.0f);
+  const uint64_t T = fadd2(X, shifter);
+  const uint64_t J = fadd2(T, pack2(-12582912.0f, -12582912.0f));
+  const uint64_t F = ffma2(J, pack2(-1.0f, -1.0f), X);
+  uint64_t P = ffma2(pack2(0.009570101276040077f, 0.009570101276040077f), F,
+                     pack2(0.05591785907745361f, 0.05591785907745361f));
+  P = ffma2(P, F, pack2(0.240247443318367f, 0.240247443318367f));
+  P = ffma2(P, F, pack2(0.6931217908859253f, 0.6931217908859253f));
+  P = ffma2(P, F, pack2(0.9999992847442627f, 0.9999992847442627f));
+  float p0, p1, t0, t1;
+  unpack2(P, p0, p1);
+  unpack2(T, t0, t1);
+  // The shifter's bit pattern is 0x4B400000 + j, so (bits << 23) == j << 23 modulo 2^32.
+  y0 = __uint_as_float(__float_as_uint(p0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(p1) + (__float_as_uint(t1) << 23));
 }
 
 }  // namespace ptx
