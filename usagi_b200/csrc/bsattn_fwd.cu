@@ -11,32 +11,31 @@
 //   Query blocks starting at or past seq_len write o = 0, lse = -inf (v4 :63-68).
 //
 // How (B200-native design, not a translation of the Triton program):
-//   * Persistent CTAs, one per SM, each running two independent query-tile "slots".  Items
-//     (bh, qb) are dealt round-robin in order of decreasing qb, so the longest causal rows go
-//     first and every CTA sees the same mix.
-//   * Warp roles (384 threads).  setmaxnreg gives the softmax warpgroups 208 registers and the
-//     control warpgroup 88; every device function is inlined, because a called function has
-//     one register allocation and cannot serve both budgets.
-//       warps 0-3  softmax + epilogue for slot 0   (thread t owns query row t of the tile)
-//       warps 4-7  softmax + epilogue for slot 1
-//       warp  8    TMA producer: Q tiles per item, K/V tiles named by col_idx into a ring
-//       warp  9    tcgen05 MMA issuer and TMEM owner
-//     The producer and MMA warps run their schedules with all 32 lanes so that addresses and
-//     descriptors are warp-uniform (the form TMA and tcgen05.mma take their operands in); only
-//     lane 0 issues the copies, MMAs and commits.
-//       warps 10-11 idle (they complete warpgroup 2 for the register re-allocation)
-//   * Tensor memory (512 columns x 128 lanes x 32 bit):
-//       slot s: S = Q K^T (fp32) at columns [256 s, 256 s + 128), O (fp32) at [256 s + 128, 256 s + 256)
-//       P (fp16, two per column) overwrites the first 64 columns of S and is the A operand of the
-//       P*V MMA straight from tensor memory.
-//   * Shared memory: Q[2] (32 KB each) + a ring of kStages K/V tiles (32 KB each), all in the
-//     128-byte-swizzled layout TMA writes and the MMA descriptors read.
-//   * MMA issue order per slot: S(0); then repeatedly PV(j), S(j+1).  Slots interleave, so while
-//     slot 0's softmax runs on S, the tensor core computes slot 1's MMAs, and vice versa.  A
-//     commit after S(j+1) therefore also certifies PV(j) done, which lets the softmax warps
-//     rescale O in place without another barrier.
-//   * Lazy rescale: the running row max m is only raised when a block's max exceeds it by more
-//     than kRescaleLog2 (P then stays <= 2^8 in fp16); the final o = O/l and lse are exact.
+//   * Persistent CTAs, one per SM.  Work items (bh, qb) are dealt round-robin in order of
+//     decreasing qb (longest causal rows first).  Each CTA streams its items' 128x128 tiles
+//     through one continuous pipeline: tile t of the CTA uses S buffer t%2, item i uses Q and O
+//     buffers i%2, so the next tile's QK^T and the next item's MMAs overlap the current softmax
+//     and the previous item's epilogue.
+//   * Warp roles (512 threads, four warpgroups; setmaxnreg re-balances the 128 launch registers):
+//       WG0 warp 0        TMA producer: Q per item, K/V tiles named by col_idx into a ring
+//       WG0 warp 1        tcgen05 MMA issuer and TMEM owner (warps 2-3 idle)
+//       WG1 (warps 4-7)   softmax for keys 0..63 of every tile   (thread t owns query row t)
+//       WG2 (warps 8-11)  softmax for keys 64..127 of every tile (same rows; the two halves of a
+//                         row exchange their maxima through shared memory)
+//       WG3 (warps 12-15) epilogue: o = O / l, lse, global stores, frees the O buffer
+//     The producer and MMA warps have the lowest warp ids: the warp schedulers favour them over
+//     the softmax warps that share their SMSPs, which keeps MMA issue off the critical path.
+//     The producer and MMA warps run their schedules with all 32 lanes so addresses and
+//     descriptors stay warp-uniform (the form TMA and tcgen05.mma take); lane 0 issues.
+//   * Tensor memory, 512 columns x 128 lanes x 32 bit:
+//       S[b] = Q K^T (fp32) at columns 128 b, b = 0, 1;  O[b] (fp32) at columns 256 + 128 b.
+//       P (fp16, two per column) overwrites S[b]: keys 0..63 at columns +0..31 (written by WG1),
+//       keys 64..127 at +64..95 (WG2); P*V reads A straight from tensor memory.
+//   * MMA order: S(0), S(1), then one back-to-back burst PV(t), S(t+2) for t = 0, 1, ...; the
+//     producer loads tiles in exactly that order (K0, K1, V0, K2, V1, ...), so the ring is
+//     consumed and released in order.
+//   * Lazy rescale: the running row max m is raised only when a block's max exceeds it by more
+//     than kRescaleLog2 (P stays <= 2^8 in fp16); the final o = O/l and lse are exact.
 //   * Every mbarrier wait is bounded (globaltimer); on expiry the CTA raises an abort flag, all
 //     roles leave their loops, in-flight TMA/MMA work is drained, TMEM is freed and
 //     BSATTN_E_TIMEOUT is left in the workspace error word.
@@ -47,6 +46,7 @@
 #include <stdint.h>
 #include <string.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "../../include/bsattn.h"
@@ -59,35 +59,46 @@ constexpr int kHd = 128;                   // head dimension
 constexpr int kStages = 4;                 // K/V ring depth
 constexpr int kTileBytes = kBlk * kHd * 2; // 32 KB fp16 tile
 constexpr int kBoxBytes = kTileBytes / 2;  // one TMA box: 128 rows x 64 columns, 128B swizzle
-constexpr int kThreads = 384;            // 3 warpgroups
-constexpr int kLoadWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kThreads = 512;              // 4 warpgroups
+constexpr int kLoadWarp = 0;
+constexpr int kMmaWarp = 1;
+constexpr int kSoftmaxWarp0 = 4;           // warps 4-7: keys 0..63, warps 8-11: keys 64..127
+constexpr int kEpiWarp0 = 12;
 constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kOCol = 256;            // O[0] column; O[1] at kOCol + 128
 constexpr float kRescaleLog2 = 8.0f;
 constexpr int kPolyEvery = 4;              // every 4th pair of exponentials runs on the FMA pipe
-// setmaxnreg budgets.  The increase draws only on the registers the block was launched with
-// (384 threads x 168 = 64512), so per SMSP lane-slot (two softmax warps + one control warp)
-// 2 * kSoftmaxRegs + kControlRegs must not exceed 3 * kLaunchRegs, or the increase never returns.
-constexpr uint32_t kLaunchRegs = 168;      // ptxas allocation for __launch_bounds__(384, 1)
-constexpr uint32_t kSoftmaxRegs = 208;
-constexpr uint32_t kControlRegs = 88;
-static_assert(2 * kSoftmaxRegs + kControlRegs <= 3 * kLaunchRegs, "register split exceeds launch");
-static_assert(kLaunchRegs * kThreads <= 65536, "launch register total");
+constexpr int kPrefetchTiles = 4;          // L2 prefetch distance, in tiles past the K loads
 constexpr int kWsInts = 64;                // workspace: int32[64]
 constexpr uint32_t kIdescQK = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescPV = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/true);
+// setmaxnreg budgets.  An increase draws only on the registers the block was launched with
+// (512 threads x 128), so per SMSP lane-slot (one warp of each warpgroup) the four budgets must
+// sum to at most 4 x kLaunchRegs, or the increase never returns.
+constexpr uint32_t kLaunchRegs = 128;      // ptxas allocation for __launch_bounds__(512, 1)
+constexpr uint32_t kSoftmaxRegs = 168;
+constexpr uint32_t kControlRegs = 88;
+constexpr uint32_t kEpilogueRegs = 88;
+static_assert(2 * kSoftmaxRegs + kControlRegs + kEpilogueRegs <= 4 * kLaunchRegs,
+              "register split exceeds the launch allocation");
+static_assert(kLaunchRegs * kThreads <= 65536, "launch register total");
 
 struct alignas(1024) SharedStorage {
   uint8_t q[2][kTileBytes];
   uint8_t kv[kStages][kTileBytes];
+  float xmax[2][2][kBlk];     // [tile parity][half][row]: partial row maxima
+  float stats[2][3][kBlk];    // [item parity]{m, l_half0, l_half1}[row]
   uint64_t q_full[2];
   uint64_t q_empty[2];
   uint64_t kv_full[kStages];
   uint64_t kv_empty[kStages];
-  uint64_t s_full[2];
-  uint64_t p_lo[2];   // P columns for keys 0..63 stored (and O rescaled if needed)
-  uint64_t p_hi[2];   // P columns for keys 64..127 stored
-  uint64_t o_full[2];
+  uint64_t s_full[2];         // S[b] computed
+  uint64_t p_rdy[2][2];       // [b][half]: P half stored in S[b] (and O rescaled if needed)
+  uint64_t pv_done[2];        // [b]: PV of a tile whose P sits in S[b] completed
+  uint64_t xchg[2][4];        // [tile parity][row quarter]: both halves posted their maxima
+  uint64_t o_full[2];         // O[b] holds a finished item
+  uint64_t o_free[2];         // epilogue done reading O[b] and its stats
+  uint64_t stats_rdy[2];      // softmax published stats[b]
   uint64_t drain;
   uint32_t tmem_base;
   int abort_flag;
@@ -141,24 +152,43 @@ __device__ __forceinline__ Item load_item(const FwdParams& p, int g, bool* csr_b
   return it;
 }
 
-struct Stream {
-  int g;
-  int stride;
-  int j;
-  int kb;
+// Walks this CTA's tiles across its active items: tile t = (item counter ii, step j).
+struct TileIter {
+  int g;      // global item index
+  int ii;     // active-item counter (buffer parity = ii & 1)
+  int j;      // step within the item
+  int t;      // tile counter (S buffer parity = t & 1)
+  int kb;     // key block of the step (producer only)
+  bool valid;
   Item it;
 };
 
-__device__ __forceinline__ bool next_active(Stream& s, const FwdParams& p, bool* csr_bad) {
+__device__ __forceinline__ bool seek_active(TileIter& x, const FwdParams& p, bool* csr_bad) {
   for (;;) {
-    s.g += s.stride;
-    if (s.g >= p.total_items) return false;
-    s.it = load_item(p, s.g, csr_bad);
-    if (s.it.n_steps > 0) {
-      s.j = 0;
-      return true;
-    }
+    x.g += gridDim.x;
+    if (x.g >= p.total_items) return false;
+    x.it = load_item(p, x.g, csr_bad);
+    if (x.it.n_steps > 0) return true;
   }
+}
+
+__device__ __forceinline__ void tile_begin(TileIter& x, const FwdParams& p, bool* csr_bad) {
+  x.g = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
+  x.ii = 0;
+  x.j = 0;
+  x.t = 0;
+  x.valid = seek_active(x, p, csr_bad);
+}
+
+__device__ __forceinline__ void tile_next(TileIter& x, const FwdParams& p, bool* csr_bad) {
+  ++x.t;
+  if (x.j + 1 < x.it.n_steps) {
+    ++x.j;
+    return;
+  }
+  x.j = 0;
+  ++x.ii;
+  x.valid = seek_active(x, p, csr_bad);
 }
 
 __device__ __forceinline__ void raise_error(const FwdParams& p, int code) {
@@ -168,7 +198,7 @@ __device__ __forceinline__ void raise_error(const FwdParams& p, int code) {
 // Bounded wait: true when the phase completed; false when this CTA aborted or the wait ran
 // past p.timeout_ns (then it raises the abort flag and the timeout error).
 __device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, SharedStorage& sh,
-                                       const FwdParams& p) {
+                                          const FwdParams& p) {
   const uint64_t t0 = ptx::globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (ptx::mbar_try_wait(bar, parity)) return true;
@@ -185,8 +215,20 @@ __device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, SharedS
 
 __device__ __forceinline__ bool wait_bar(uint32_t bar, uint32_t parity, SharedStorage& sh,
                                          const FwdParams& p) {
-  if (ptx::mbar_try_wait(bar, parity)) return true;
+  if (ptx::mbar_test_wait(bar, parity)) return true;  // completed phases cost ~14 cycles
   return wait_slow(bar, parity, sh, p);
+}
+
+// Bounded wait executed by a whole warp; the result is the same on every lane.
+__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, SharedStorage& sh,
+                                          const FwdParams& p) {
+  return __all_sync(0xffffffffu, wait_bar(bar, parity, sh, p));
+}
+
+// Wait used by the producer and MMA roles, which run on lane 0 alone.
+__device__ __forceinline__ bool wait_ctl(uint32_t bar, uint32_t parity, SharedStorage& sh,
+                                         const FwdParams& p) {
+  return wait_bar(bar, parity, sh, p);
 }
 
 // Drain wait used during teardown: ignores the abort flag, still bounded in time.
@@ -201,27 +243,17 @@ __device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity, const 
   }
 }
 
-// Bounded wait executed by a whole warp; the result is the same on every lane.
-__device__ __forceinline__ bool wait_warp(uint32_t bar, uint32_t parity, SharedStorage& sh,
-                                          const FwdParams& p) {
-  return __all_sync(0xffffffffu, wait_bar(bar, parity, sh, p));
-}
-
 // ------------------------------------------------------------------------------------------
-// Producer warp: mirrors the MMA issue order exactly -- S(first) of slot 0 and 1, then per slot
-// "V(j), K(j+1)" -- so the ring holds tiles in the order the MMAs consume them.  The whole warp
-// runs the control flow (so coordinates stay warp-uniform, which is what the TMA instruction
-// consumes); lane 0 alone issues the copies.
+// Producer warp.  Load order = MMA consumption order: K(0), K(1), then V(t), K(t+2) for
+// t = 0, 1, ...; Q of an item right before its first K.  Lane 0 issues the copies.
 // ------------------------------------------------------------------------------------------
 __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CUtensorMap* tk,
                               const CUtensorMap* tv, const FwdParams& p, bool leader) {
   bool csr_bad = false;
   const uint64_t pol_kv = ptx::policy_evict_last();
   const uint64_t pol_q = ptx::policy_evict_first();
-  Stream st[2];
-  bool has[2];
-  uint32_t qe_phase[2] = {0, 0};
-  uint32_t q_issued = 0, q_last_parity = 0;    // bit s: slot s
+  TileIter ks, vs;  // ks runs two tiles ahead of vs
+  uint32_t q_issued = 0, q_last_parity = 0;  // bit b: Q buffer b
   int stage = 0;
   uint32_t kv_phase = 0;
   uint32_t kv_issued = 0;       // bit i: stage i received at least one load
@@ -235,37 +267,34 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
   auto load_tile = [&](const CUtensorMap* map, int row) -> bool {
     const uint32_t empty = kv_empty0 + stage * 8;
     const uint32_t full = kv_full0 + stage * 8;
-    if (!wait_warp(empty, kv_phase ^ 1u, sh, p)) return false;
+    if (!wait_ctl(empty, kv_phase ^ 1u, sh, p)) return false;
     if (leader) {
       const uint32_t dst = kv_smem0 + stage * kTileBytes;
       ptx::mbar_expect_tx(full, kTileBytes);
-      ptx::tma_load_2d(dst, map, full, 0, row, pol_kv);
-      ptx::tma_load_2d(dst + kBoxBytes, map, full, 64, row, pol_kv);
+      ptx::tma_load_3d(dst, map, full, 0, row, 0, pol_kv);
     }
-    __syncwarp();
     kv_issued |= 1u << stage;
     kv_last_parity = (kv_last_parity & ~(1u << stage)) | (kv_phase << stage);
     if (++stage == kStages) stage = 0, kv_phase ^= 1u;
     return true;
   };
-  auto load_S = [&](int s) -> bool {
-    Stream& x = st[s];
+  // K of tile x (and Q first when x starts an item); remembers the key block for its V.
+  auto load_K = [&](TileIter& x) -> bool {
     const int head_row0 = x.it.bh * p.T;
     if (x.j == 0) {
-      const uint32_t empty = ptx::smem_u32(&sh.q_empty[s]);
-      const uint32_t full = ptx::smem_u32(&sh.q_full[s]);
-      if (!wait_warp(empty, qe_phase[s] ^ 1u, sh, p)) return false;
+      const int b = x.ii & 1;
+      const uint32_t empty = ptx::smem_u32(&sh.q_empty[b]);
+      const uint32_t full = ptx::smem_u32(&sh.q_full[b]);
+      const uint32_t ph = (static_cast<uint32_t>(x.ii) >> 1) & 1u;
+      if (!wait_ctl(empty, ph ^ 1u, sh, p)) return false;
       if (leader) {
-        const uint32_t dst = q_smem0 + s * kTileBytes;
+        const uint32_t dst = q_smem0 + b * kTileBytes;
         const int row = head_row0 + x.it.qb * kBlk;
         ptx::mbar_expect_tx(full, kTileBytes);
-        ptx::tma_load_2d(dst, tq, full, 0, row, pol_q);
-        ptx::tma_load_2d(dst + kBoxBytes, tq, full, 64, row, pol_q);
+        ptx::tma_load_3d(dst, tq, full, 0, row, 0, pol_q);
       }
-      __syncwarp();
-      q_issued |= 1u << s;
-      q_last_parity = (q_last_parity & ~(1u << s)) | (qe_phase[s] << s);
-      qe_phase[s] ^= 1u;
+        q_issued |= 1u << b;
+      q_last_parity = (q_last_parity & ~(1u << b)) | (ph << b);
     }
     int kb = x.it.qb;  // diagonal
     if (x.j < x.it.n_steps - 1) {
@@ -278,52 +307,71 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
     x.kb = kb;
     return load_tile(tk, head_row0 + kb * kBlk);
   };
-  auto load_V = [&](int s) -> bool { return load_tile(tv, st[s].it.bh * p.T + st[s].kb * kBlk); };
 
-#pragma unroll
-  for (int s = 0; s < 2; ++s) {
-    st[s].g = 2 * blockIdx.x + s - 2 * gridDim.x;
-    st[s].stride = 2 * gridDim.x;
-    has[s] = next_active(st[s], p, &csr_bad);
-    if (has[s] && ok) ok = load_S(s);
-  }
-  while (ok && (has[0] || has[1])) {
-#pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      if (!ok || !has[s]) continue;
-      ok = load_V(s);
-      if (!ok) continue;
-      if (st[s].j + 1 < st[s].it.n_steps) {
-        ++st[s].j;
-        ok = load_S(s);
-      } else {
-        has[s] = next_active(st[s], p, &csr_bad);
-        if (has[s]) ok = load_S(s);
-      }
+  // vs trails ks by two tiles; its key block is read again from col_idx (an L1 hit).
+  auto key_block = [&](const TileIter& x) -> int {
+    int kb = x.it.qb;
+    if (x.j < x.it.n_steps - 1) {
+      kb = __ldg(p.col_idx + (long long)x.it.bh * p.ci_stride + x.it.row_start + x.j);
+      if (kb < 0 || kb >= p.nqb) kb = x.it.qb;
     }
+    return kb;
+  };
+  // pf runs kPrefetchTiles ahead of ks and pulls each tile's K, V (and Q at an item start)
+  // into L2, so the shared-memory loads that follow hit L2 instead of HBM.
+  TileIter pf;
+  tile_begin(pf, p, nullptr);
+  auto prefetch = [&]() {
+    if (!pf.valid) return;
+    if (leader) {
+      const int head_row0 = pf.it.bh * p.T;
+      if (pf.j == 0) ptx::tma_prefetch_l2_3d(tq, 0, head_row0 + pf.it.qb * kBlk, 0);
+      const int row = head_row0 + key_block(pf) * kBlk;
+      ptx::tma_prefetch_l2_3d(tk, 0, row, 0);
+      ptx::tma_prefetch_l2_3d(tv, 0, row, 0);
+    }
+    tile_next(pf, p, nullptr);
+  };
+  for (int i = 0; i < kPrefetchTiles + 2; ++i) prefetch();
+
+  tile_begin(ks, p, &csr_bad);
+  tile_begin(vs, p, nullptr);
+  for (int i = 0; i < 2 && ok && ks.valid; ++i) {
+    ok = load_K(ks);
+    tile_next(ks, p, &csr_bad);
+  }
+  while (ok && vs.valid) {
+    ok = load_tile(tv, vs.it.bh * p.T + key_block(vs) * kBlk);
+    if (!ok) break;
+    if (ks.valid) {
+      ok = load_K(ks);
+      tile_next(ks, p, &csr_bad);
+    }
+    prefetch();
+    tile_next(vs, p, nullptr);
   }
   if (csr_bad && leader) raise_error(p, BSATTN_E_CSR);
   if (!ok) {
     // Aborted: make sure no TMA write is still landing in shared memory before the CTA exits.
     for (int i = 0; i < kStages; ++i)
       if ((kv_issued >> i) & 1u) wait_drain(kv_full0 + i * 8, (kv_last_parity >> i) & 1u, p);
-    for (int s = 0; s < 2; ++s)
-      if ((q_issued >> s) & 1u)
-        wait_drain(ptx::smem_u32(&sh.q_full[s]), (q_last_parity >> s) & 1u, p);
+    for (int b = 0; b < 2; ++b)
+      if ((q_issued >> b) & 1u)
+        wait_drain(ptx::smem_u32(&sh.q_full[b]), (q_last_parity >> b) & 1u, p);
   }
 }
 
 // ------------------------------------------------------------------------------------------
-// MMA warp: the whole warp runs the schedule and builds the descriptors (warp-uniform values);
-// lane 0 issues every tcgen05.mma and tcgen05.commit, so one thread owns all MMA completions.
-// Descriptors are formed once and advanced by adding (byte offset >> 4) to the start-address
-// field, which never carries out of its 14 bits inside the 227 KB of shared memory.
+// MMA warp: S(0), S(1), then per tile one burst "PV(t), S(t+2)".  tcgen05.mma issue blocks at the
+// tensor pipe's execution rate (its queue holds only a couple of instructions), so the pipe
+// drains whenever this warp pauses; every wait for a burst is therefore done before its first
+// MMA, and the sixteen MMAs then go out back to back.  The whole warp runs the schedule and builds
+// the descriptors (warp-uniform values); lane 0 issues every tcgen05.mma and tcgen05.commit, so
+// one thread owns all MMA completions.  Descriptors are advanced by adding (byte offset >> 4) to
+// the start-address field, which never carries out of its 14 bits inside 227 KB of shared memory.
 // ------------------------------------------------------------------------------------------
 __device__ void mma_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem, bool leader) {
-  Stream st[2];
-  bool has[2];
-  uint32_t qf_phase[2] = {0, 0};
-  uint32_t pr_phase[2] = {0, 0};
+  TileIter ss, pv;  // ss runs two tiles ahead of pv
   int stage = 0;
   uint32_t kv_phase = 0;
   const uint64_t q_desc0 = ptx::sdesc_sw128(ptx::smem_u32(sh.q[0]), 16, 1024);
@@ -333,96 +381,245 @@ __device__ void mma_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem, b
   const uint32_t kv_empty0 = ptx::smem_u32(&sh.kv_empty[0]);
   bool ok = true;
 
-  auto issue_S = [&](int s) -> bool {
-    Stream& x = st[s];
-    if (x.j == 0) {
-      if (!wait_warp(ptx::smem_u32(&sh.q_full[s]), qf_phase[s], sh, p)) return false;
-      qf_phase[s] ^= 1u;
-    }
-    if (!wait_warp(kv_full0 + stage * 8, kv_phase, sh, p)) return false;
-    ptx::tc_fence_after();
-    const uint64_t qd = q_desc0 + static_cast<uint32_t>((s * kTileBytes) >> 4);
-    const uint64_t kd = k_desc0 + static_cast<uint32_t>((stage * kTileBytes) >> 4);
-    const uint32_t d = tmem + s * 256;
+  // Waits that must precede S(x): its Q (first tile of an item) and its K tile at `kstage`.
+  auto wait_S = [&](const TileIter& x, int kstage, uint32_t kphase) -> bool {
+    if (x.j == 0 &&
+        !wait_ctl(ptx::smem_u32(&sh.q_full[x.ii & 1]), (static_cast<uint32_t>(x.ii) >> 1) & 1u, sh, p))
+      return false;
+    return wait_ctl(kv_full0 + kstage * 8, kphase, sh, p);
+  };
+  auto issue_S = [&](const TileIter& x, int kstage) {
+    const int qb = x.ii & 1;
+    const int sb = x.t & 1;
+    const uint64_t qd = q_desc0 + static_cast<uint32_t>((qb * kTileBytes) >> 4);
+    const uint64_t kd = k_desc0 + static_cast<uint32_t>((kstage * kTileBytes) >> 4);
+    const uint32_t d = tmem + sb * 128;
     if (leader) {
 #pragma unroll
       for (int kk = 0; kk < kHd / 16; ++kk) {
         const uint32_t off = ((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4;
         ptx::mma_ss(d, qd + off, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
       }
-      ptx::tc_commit(kv_empty0 + stage * 8);
-      ptx::tc_commit(ptx::smem_u32(&sh.s_full[s]));
-      if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.q_empty[s]));
+      ptx::tc_commit(kv_empty0 + kstage * 8);
+      ptx::tc_commit(ptx::smem_u32(&sh.s_full[sb]));
+      if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.q_empty[qb]));
     }
-    __syncwarp();
-    if (++stage == kStages) stage = 0, kv_phase ^= 1u;
-    return true;
   };
-  auto issue_PV = [&](int s) -> bool {
-    Stream& x = st[s];
-    if (!wait_warp(kv_full0 + stage * 8, kv_phase, sh, p)) return false;
-    const uint64_t vd = v_desc0 + static_cast<uint32_t>((stage * kTileBytes) >> 4);
-    const uint32_t d = tmem + s * 256 + 128;
-    const uint32_t a = tmem + s * 256;
-    // P arrives in two halves (keys 0..63, 64..127); the first four K-steps start as soon as the
-    // first half is in tensor memory.
-#pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const uint32_t bar = ptx::smem_u32(half == 0 ? &sh.p_lo[s] : &sh.p_hi[s]);
-      if (!wait_warp(bar, pr_phase[s], sh, p)) return false;
-      ptx::tc_fence_after();
-      if (leader) {
-#pragma unroll
-        for (int k4 = 0; k4 < 4; ++k4) {
-          const int kk = half * 4 + k4;
-          // V is [key][d] with d contiguous: MN-major B operand.  One K step = 16 keys = two
-          // 8-row swizzle atoms (2 KB); the second 64-column half of d sits one TMA box later.
-          ptx::mma_ts(d, a + kk * 8, vd + static_cast<uint32_t>((kk * 2048) >> 4), kIdescPV,
-                      (x.j > 0 || kk > 0) ? 1u : 0u);
-        }
-      }
-      __syncwarp();
-    }
-    pr_phase[s] ^= 1u;
-    if (leader) {
-      ptx::tc_commit(kv_empty0 + stage * 8);
-      if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.o_full[s]));
-    }
-    __syncwarp();
-    if (++stage == kStages) stage = 0, kv_phase ^= 1u;
-    return true;
+  auto advance = [&](int& st, uint32_t& ph) {
+    if (++st == kStages) st = 0, ph ^= 1u;
   };
 
-#pragma unroll
-  for (int s = 0; s < 2; ++s) {
-    st[s].g = 2 * blockIdx.x + s - 2 * gridDim.x;
-    st[s].stride = 2 * gridDim.x;
-    has[s] = next_active(st[s], p, nullptr);
-    if (has[s] && ok) ok = issue_S(s);
+  tile_begin(ss, p, nullptr);
+  tile_begin(pv, p, nullptr);
+  for (int i = 0; i < 2 && ok && ss.valid; ++i) {
+    ok = wait_S(ss, stage, kv_phase);
+    if (!ok) break;
+    ptx::tc_fence_after();
+    issue_S(ss, stage);
+    advance(stage, kv_phase);
+    tile_next(ss, p, nullptr);
   }
-  while (ok && (has[0] || has[1])) {
+  while (ok && pv.valid) {
+    // ---- every wait of the burst first
+    const int vstage = stage;
+    const uint32_t vphase = kv_phase;
+    int kstage = vstage;
+    uint32_t kphase = vphase;
+    advance(kstage, kphase);
+    const int ob = pv.ii & 1;
+    const int sb = pv.t & 1;
+    const uint32_t tph = (static_cast<uint32_t>(pv.t) >> 1) & 1u;
+    ok = wait_ctl(kv_full0 + vstage * 8, vphase, sh, p);
+    if (ok && pv.j == 0 && pv.ii >= 2)  // O[ob] read out by the epilogue of item ii-2
+      ok = wait_ctl(ptx::smem_u32(&sh.o_free[ob]), ((static_cast<uint32_t>(pv.ii) >> 1) + 1u) & 1u,
+                     sh, p);
+    if (ok) ok = wait_ctl(ptx::smem_u32(&sh.p_rdy[sb][0]), tph, sh, p);
+    if (ok) ok = wait_ctl(ptx::smem_u32(&sh.p_rdy[sb][1]), tph, sh, p);
+    if (ok && ss.valid) ok = wait_S(ss, kstage, kphase);
+    if (!ok) break;
+    ptx::tc_fence_after();
+    // ---- PV(t): O[ob] (+)= P(t) V(t)
+    const uint64_t vd = v_desc0 + static_cast<uint32_t>((vstage * kTileBytes) >> 4);
+    const uint32_t d = tmem + kOCol + ob * 128;
+    const uint32_t a = tmem + sb * 128;
+    if (leader) {
 #pragma unroll
-    for (int s = 0; s < 2; ++s) {
-      if (!ok || !has[s]) continue;
-      ok = issue_PV(s);
-      if (!ok) continue;
-      if (st[s].j + 1 < st[s].it.n_steps) {
-        ++st[s].j;
-        ok = issue_S(s);
-      } else {
-        has[s] = next_active(st[s], p, nullptr);
-        if (has[s]) ok = issue_S(s);
+      for (int kk = 0; kk < kBlk / 16; ++kk) {
+        // V is [key][d] with d contiguous: MN-major B operand.  One K step = 16 keys = two
+        // 8-row swizzle atoms (2 KB); the second 64-column half of d sits one TMA box later.
+        // P keys 0..63 sit at columns +0..31 of S[sb], keys 64..127 at +64..95.
+        ptx::mma_ts(d, a + (kk >> 2) * 64 + (kk & 3) * 8,
+                    vd + static_cast<uint32_t>((kk * 2048) >> 4), kIdescPV,
+                    (pv.j > 0 || kk > 0) ? 1u : 0u);
       }
+      ptx::tc_commit(kv_empty0 + vstage * 8);
+      ptx::tc_commit(ptx::smem_u32(&sh.pv_done[sb]));
+      if (pv.j == pv.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.o_full[ob]));
     }
+    // ---- S(t+2) straight after, into the S buffer PV(t) just read
+    if (ss.valid) issue_S(ss, kstage);
+    stage = kstage;
+    kv_phase = kphase;
+    if (ss.valid) {
+      advance(stage, kv_phase);
+      tile_next(ss, p, nullptr);
+    }
+    tile_next(pv, p, nullptr);
   }
 }
 
 // ------------------------------------------------------------------------------------------
-// Softmax + epilogue warpgroup for one slot.  Thread t owns query row t of the tile and the
-// TMEM lane t (warp w of the group may only touch lanes 32*(w%4) .. +31).
+// Softmax warpgroup `half` (0: keys 0..63, 1: keys 64..127 of every tile).  Thread t owns query
+// row t and TMEM lane t (warp w may only touch lanes 32*(w%4) .. +31); the warp pair (w, w+4)
+// covers the same 32 rows and exchanges partial maxima through shared memory (an mbarrier per
+// row quarter and tile parity, so the exchange wait is bounded like every other wait).
 // ------------------------------------------------------------------------------------------
-__device__ __forceinline__ void store_row_f32(const FwdParams& p, size_t row, const float* v32,
-                                              int col0, float mul, bool valid) {
+__device__ void softmax_role(SharedStorage& sh, const FwdParams& p, int half, uint32_t tmem) {
+  const int t = threadIdx.x - kSoftmaxWarp0 * 32 - half * 128;
+  const int wq = t >> 5;
+  const uint32_t lane_addr = tmem + (static_cast<uint32_t>(wq * 32) << 16);
+  const float sl2 = p.scale_log2;
+  int tile = 0;
+  int ii = 0;
+
+  for (int g = blockIdx.x; g < p.total_items; g += gridDim.x) {
+    const Item it = load_item(p, g, nullptr);
+    if (it.n_steps == 0) continue;  // the epilogue warpgroup writes inactive items
+    const int ob = ii & 1;
+    const bool row_valid = it.qb * kBlk + t < it.seq_len;
+    float m_run = -1e30f;  // v4 :74
+    float l_run = 0.0f;
+
+    for (int j = 0; j < it.n_steps; ++j, ++tile) {
+      const int sb = tile & 1;
+      const uint32_t s_addr = lane_addr + sb * 128 + half * 64;
+      if (!wait_warp(ptx::smem_u32(&sh.s_full[sb]), (static_cast<uint32_t>(tile) >> 1) & 1u, sh, p))
+        return;
+      ptx::tc_fence_after();
+      uint32_t sr[64];
+      ptx::tmem_ld32(s_addr + 0, sr + 0);
+      ptx::tmem_ld32(s_addr + 32, sr + 32);
+      ptx::tmem_wait_ld();
+#pragma unroll
+      for (int c = 0; c < 64; ++c) ptx::reg_fence(sr[c]);
+      float s[64];
+#pragma unroll
+      for (int c = 0; c < 64; ++c) s[c] = __uint_as_float(sr[c]);
+
+      // Key 64*half + c is masked when c >= n_keep: the causal diagonal keeps key <= t (v4 :111;
+      // with t valid that also keeps key < seq_len, v4 :112), an invalid row keeps nothing (:93).
+      const bool diag = (j == it.n_steps - 1);
+      const int n_keep = !row_valid ? 0 : (diag ? min(max(t + 1 - 64 * half, 0), 64) : 64);
+      if (n_keep < 64) {
+#pragma unroll
+        for (int c = 0; c < 64; ++c) s[c] = (c < n_keep) ? s[c] : -INFINITY;
+      }
+      float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
+#pragma unroll
+      for (int c = 4; c < 60; c += 8) {
+        a0 = ptx::fmax3(a0, s[c + 0], s[c + 1]);
+        a1 = ptx::fmax3(a1, s[c + 2], s[c + 3]);
+        a2 = ptx::fmax3(a2, s[c + 4], s[c + 5]);
+        a3 = ptx::fmax3(a3, s[c + 6], s[c + 7]);
+      }
+      a0 = ptx::fmax3(a0, s[60], s[61]);
+      a1 = ptx::fmax3(a1, s[62], s[63]);
+      const float pmax = ptx::fmax3(a0, a1, fmaxf(a2, a3));
+      // Row max over both halves (raw scores; scale > 0 commutes with max).
+      sh.xmax[tile & 1][half][t] = pmax;
+      ptx::mbar_arrive(ptx::smem_u32(&sh.xchg[tile & 1][wq]));
+      if (!wait_warp(ptx::smem_u32(&sh.xchg[tile & 1][wq]), (static_cast<uint32_t>(tile) >> 1) & 1u,
+                     sh, p))
+        return;
+      const float m_cand = fmaxf(pmax, sh.xmax[tile & 1][half ^ 1][t]) * sl2;
+
+      // Both halves see the same maxima, so they take the same rescale decision.
+      float alpha = 1.0f;
+      bool rescale = false;
+      if (j == 0) {
+        m_run = fmaxf(m_run, m_cand);
+      } else {
+        const bool need = m_cand > m_run + kRescaleLog2;
+        rescale = __any_sync(0xffffffffu, need);
+        if (rescale) {
+          const float m_new = fmaxf(m_run, m_cand);
+          alpha = ptx::ex2(m_run - m_new);
+          l_run *= alpha;
+          m_run = m_new;
+        }
+      }
+      const uint64_t sc2 = ptx::pack2(sl2, sl2);
+      const uint64_t nm2 = ptx::pack2(-m_run, -m_run);
+      uint64_t acc0 = 0, acc1 = 0;
+      uint32_t pk[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) {
+        const uint64_t x2 = ptx::ffma2(ptx::pack2(s[2 * i], s[2 * i + 1]), sc2, nm2);
+        float x0, x1, p0, p1;
+        ptx::unpack2(x2, x0, x1);
+        if (kPolyEvery > 0 && (i % kPolyEvery) == kPolyEvery - 1) {
+          ptx::exp2_poly_pair(x0, x1, p0, p1);
+        } else {
+          p0 = ptx::ex2(x0);
+          p1 = ptx::ex2(x1);
+        }
+        const uint64_t p2 = ptx::pack2(p0, p1);
+        if (i & 1) acc1 = ptx::fadd2(acc1, p2); else acc0 = ptx::fadd2(acc0, p2);
+        __half2 hv = __floats2half2_rn(p0, p1);
+        pk[i] = *reinterpret_cast<uint32_t*>(&hv);
+      }
+      ptx::tmem_st32(s_addr, pk);
+      if (rescale) {
+        // O must include PV(tile-1) before it is scaled.  pv_done[b] completes once per tile that
+        // uses S[b]; PV(tile-3) (same buffer) completed before S(tile-1) was issued, and PV(tile+1)
+        // cannot run before this tile's P exists, so the parity below is unambiguous.
+        const uint32_t pb = static_cast<uint32_t>(tile - 1) & 1u;
+        if (!wait_warp(ptx::smem_u32(&sh.pv_done[pb]), (static_cast<uint32_t>(tile - 1) >> 1) & 1u,
+                       sh, p))
+          return;
+        ptx::tc_fence_after();
+        const uint32_t o_addr = lane_addr + kOCol + ob * 128 + half * 64;
+#pragma unroll 1
+        for (int c = 0; c < 2; ++c) {
+          uint32_t orow[32];
+          ptx::tmem_ld32(o_addr + c * 32, orow);
+          ptx::tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            ptx::reg_fence(orow[i]);
+            orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
+          }
+          ptx::tmem_st32(o_addr + c * 32, orow);
+        }
+      }
+      ptx::tmem_wait_st();
+      ptx::tc_fence_before();
+      ptx::mbar_arrive(ptx::smem_u32(&sh.p_rdy[sb][half]));
+      float l0, l1;
+      ptx::unpack2(ptx::fadd2(acc0, acc1), l0, l1);
+      l_run += l0 + l1;
+    }
+
+    // Publish the row statistics of item ii for the epilogue.  stats[ob] was last read by the
+    // epilogue of item ii-2, which released O[ob] through o_free[ob].
+    if (ii >= 2) {
+      if (!wait_warp(ptx::smem_u32(&sh.o_free[ob]), ((static_cast<uint32_t>(ii) >> 1) + 1u) & 1u,
+                     sh, p))
+        return;
+    }
+    if (half == 0) sh.stats[ob][0][t] = m_run;
+    sh.stats[ob][1 + half][t] = l_run;
+    ptx::mbar_arrive(ptx::smem_u32(&sh.stats_rdy[ob]));
+    ++ii;
+  }
+}
+
+// ------------------------------------------------------------------------------------------
+// Epilogue warpgroup: o = O / l (v4 :126-133), lse = m ln2 + ln l (v4 :134-136); rows of
+// query blocks past seq_len are written as o = 0, lse = -inf (v4 :63-68).
+// ------------------------------------------------------------------------------------------
+__device__ __forceinline__ void store_row32(const FwdParams& p, size_t row, int col0,
+                                            const float* v32, float mul, bool valid) {
   uint4 pk[4];
   uint32_t* w = reinterpret_cast<uint32_t*>(pk);
 #pragma unroll
@@ -442,148 +639,34 @@ __device__ __forceinline__ void store_row_f32(const FwdParams& p, size_t row, co
   for (int i = 0; i < 4; ++i) dst[i] = pk[i];
 }
 
-__device__ void softmax_role(SharedStorage& sh, const FwdParams& p, int slot, uint32_t tmem) {
-  const int t = threadIdx.x - slot * 128;
-  const int wq = (threadIdx.x >> 5) & 3;
+__device__ void epilogue_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem) {
+  const int t = threadIdx.x - kEpiWarp0 * 32;
+  const int wq = t >> 5;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(wq * 32) << 16);
-  const uint32_t s_addr = lane_addr + slot * 256;
-  const uint32_t o_addr = s_addr + 128;
-  const uint32_t s_full = ptx::smem_u32(&sh.s_full[slot]);
-  const uint32_t p_lo = ptx::smem_u32(&sh.p_lo[slot]);
-  const uint32_t p_hi = ptx::smem_u32(&sh.p_hi[slot]);
-  const uint32_t o_full = ptx::smem_u32(&sh.o_full[slot]);
-  uint32_t sf_phase = 0, of_phase = 0;
-  const float sl2 = p.scale_log2;
-
-  for (int g = 2 * blockIdx.x + slot; g < p.total_items; g += 2 * gridDim.x) {
+  int ii = 0;
+  for (int g = blockIdx.x; g < p.total_items; g += gridDim.x) {
     const Item it = load_item(p, g, nullptr);
     const int q_pos = it.qb * kBlk + t;
     const size_t row = static_cast<size_t>(it.bh) * p.T + q_pos;
-    if (it.n_steps == 0) {  // query block entirely past seq_len (v4 :63-68)
+    if (it.n_steps == 0) {
       float z[32];
 #pragma unroll
       for (int i = 0; i < 32; ++i) z[i] = 0.0f;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) store_row_f32(p, row, z, c * 32, 0.0f, false);
+      for (int c = 0; c < 4; ++c) store_row32(p, row, c * 32, z, 0.0f, false);
       if (p.lse) p.lse[row] = -INFINITY;
       continue;
     }
-    const bool row_valid = q_pos < it.seq_len;
-    float m_run = -1e30f;  // v4 :74
-    float l_run = 0.0f;
-
-    for (int j = 0; j < it.n_steps; ++j) {
-      bool ok = wait_bar(s_full, sf_phase, sh, p);
-      if (!__all_sync(0xffffffffu, ok)) return;
-      sf_phase ^= 1u;
-      ptx::tc_fence_after();
-      uint32_t sr[128];
-      ptx::tmem_ld32(s_addr + 0, sr + 0);
-      ptx::tmem_ld32(s_addr + 32, sr + 32);
-      ptx::tmem_ld32(s_addr + 64, sr + 64);
-      ptx::tmem_ld32(s_addr + 96, sr + 96);
-      ptx::tmem_wait_ld();
-#pragma unroll
-      for (int c = 0; c < 128; ++c) ptx::reg_fence(sr[c]);
-      float s[128];
-#pragma unroll
-      for (int c = 0; c < 128; ++c) s[c] = __uint_as_float(sr[c]);
-
-      // Keys c >= n_keep are masked: the causal diagonal keeps c <= t (v4 :111; with t valid
-      // that also keeps key < seq_len, v4 :112), an invalid query row keeps nothing (v4 :93).
-      const bool diag = (j == it.n_steps - 1);
-      const int n_keep = !row_valid ? 0 : (diag ? t + 1 : 128);
-      if (n_keep < 128) {
-#pragma unroll
-        for (int c = 0; c < 128; ++c) s[c] = (c < n_keep) ? s[c] : -INFINITY;
-      }
-      // Row max of the raw scores (scale > 0 commutes with max), three inputs per instruction.
-      float a0 = s[0], a1 = s[1], a2 = s[2], a3 = s[3];
-#pragma unroll
-      for (int c = 4; c < 124; c += 8) {
-        a0 = ptx::fmax3(a0, s[c + 0], s[c + 1]);
-        a1 = ptx::fmax3(a1, s[c + 2], s[c + 3]);
-        a2 = ptx::fmax3(a2, s[c + 4], s[c + 5]);
-        a3 = ptx::fmax3(a3, s[c + 6], s[c + 7]);
-      }
-      a0 = ptx::fmax3(a0, s[124], s[125]);
-      a1 = ptx::fmax3(a1, s[126], s[127]);
-      const float m_cand = ptx::fmax3(a0, a1, fmaxf(a2, a3)) * sl2;
-      // Decide the new running max before touching O: P is computed against it, and O is
-      // rescaled before the first half of P is released to the MMA.
-      float alpha = 1.0f;
-      bool rescale = false;
-      if (j == 0) {
-        m_run = fmaxf(m_run, m_cand);
-      } else {
-        const bool need = m_cand > m_run + kRescaleLog2;
-        rescale = __any_sync(0xffffffffu, need);
-        if (rescale) {
-          const float m_new = fmaxf(m_run, m_cand);
-          alpha = ptx::ex2(m_run - m_new);
-          l_run *= alpha;
-          m_run = m_new;
-        }
-      }
-      // p = 2^(s*scale - m) on pairs: one packed FMA per pair, MUFU for most exponentials and
-      // the FMA-pipe polynomial for every kPolyEvery-th pair; the row sum l accumulates the
-      // fp32 p (v4 :99) in packed adds; P is stored as fp16 pairs (v4 :103).
-      const uint64_t sc2 = ptx::pack2(sl2, sl2);
-      const uint64_t nm2 = ptx::pack2(-m_run, -m_run);
-      uint64_t acc0 = 0, acc1 = 0;
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        uint32_t pk[32];
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int c = 64 * h + 2 * i;
-          const uint64_t x2 = ptx::ffma2(ptx::pack2(s[c], s[c + 1]), sc2, nm2);
-          float x0, x1, p0, p1;
-          ptx::unpack2(x2, x0, x1);
-          if (kPolyEvery > 0 && (i % kPolyEvery) == kPolyEvery - 1) {
-            ptx::exp2_poly_pair(x0, x1, p0, p1);
-          } else {
-            p0 = ptx::ex2(x0);
-            p1 = ptx::ex2(x1);
-          }
-          const uint64_t p2 = ptx::pack2(p0, p1);
-          if (i & 1) acc1 = ptx::fadd2(acc1, p2); else acc0 = ptx::fadd2(acc0, p2);
-          __half2 hv = __floats2half2_rn(p0, p1);
-          pk[i] = *reinterpret_cast<uint32_t*>(&hv);
-        }
-        ptx::tmem_st32(s_addr + 32 * h, pk);
-        if (h == 0 && rescale) {
-          // O holds the sum through PV(j-1), which completed before S(j) was committed.
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t orow[32];
-            ptx::tmem_ld32(o_addr + c * 32, orow);
-            ptx::tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) {
-              ptx::reg_fence(orow[i]);
-              orow[i] = __float_as_uint(__uint_as_float(orow[i]) * alpha);
-            }
-            ptx::tmem_st32(o_addr + c * 32, orow);
-          }
-        }
-        ptx::tmem_wait_st();
-        ptx::tc_fence_before();
-        ptx::mbar_arrive(h == 0 ? p_lo : p_hi);
-      }
-      float l0, l1, l2, l3;
-      ptx::unpack2(ptx::fadd2(acc0, acc1), l0, l1);
-      (void)l2;
-      (void)l3;
-      l_run += l0 + l1;
-    }
-
-    // Epilogue: o = O / l (v4 :126-133), lse = m ln2 + ln l (v4 :134-136).
-    bool ok = wait_bar(o_full, of_phase, sh, p);
-    if (!__all_sync(0xffffffffu, ok)) return;
-    of_phase ^= 1u;
+    const int ob = ii & 1;
+    const uint32_t ph = (static_cast<uint32_t>(ii) >> 1) & 1u;
+    if (!wait_warp(ptx::smem_u32(&sh.o_full[ob]), ph, sh, p)) return;
+    if (!wait_warp(ptx::smem_u32(&sh.stats_rdy[ob]), ph, sh, p)) return;
     ptx::tc_fence_after();
+    const bool row_valid = q_pos < it.seq_len;
+    const float m_run = sh.stats[ob][0][t];
+    const float l_run = sh.stats[ob][1][t] + sh.stats[ob][2][t];
     const float inv_l = l_run > 0.0f ? 1.0f / l_run : 1.0f;
+    const uint32_t o_addr = lane_addr + kOCol + ob * 128;
 #pragma unroll 1
     for (int c = 0; c < 4; ++c) {
       uint32_t orow[32];
@@ -595,13 +678,15 @@ __device__ void softmax_role(SharedStorage& sh, const FwdParams& p, int slot, ui
         ptx::reg_fence(orow[i]);
         of[i] = __uint_as_float(orow[i]);
       }
-      store_row_f32(p, row, of, c * 32, inv_l, row_valid);
+      store_row32(p, row, c * 32, of, inv_l, row_valid);
     }
     if (p.lse) {
-      const float lse = (row_valid && l_run > 0.0f) ? m_run * 0.69314718055994531f + logf(l_run)
-                                                    : -INFINITY;
-      p.lse[row] = lse;
+      p.lse[row] = (row_valid && l_run > 0.0f) ? m_run * 0.69314718055994531f + logf(l_run)
+                                               : -INFINITY;
     }
+    ptx::tc_fence_before();
+    ptx::mbar_arrive(ptx::smem_u32(&sh.o_free[ob]));
+    ++ii;
   }
 }
 
@@ -616,18 +701,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < 2; ++s) {
-      ptx::mbar_init(ptx::smem_u32(&sh.q_full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&sh.q_empty[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&sh.s_full[s]), 1);
-      ptx::mbar_init(ptx::smem_u32(&sh.p_lo[s]), 128);
-      ptx::mbar_init(ptx::smem_u32(&sh.p_hi[s]), 128);
-      ptx::mbar_init(ptx::smem_u32(&sh.o_full[s]), 1);
+    for (int b = 0; b < 2; ++b) {
+      ptx::mbar_init(ptx::smem_u32(&sh.q_full[b]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sh.q_empty[b]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sh.s_full[b]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sh.p_rdy[b][0]), 128);
+      ptx::mbar_init(ptx::smem_u32(&sh.p_rdy[b][1]), 128);
+      ptx::mbar_init(ptx::smem_u32(&sh.o_full[b]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sh.o_free[b]), 128);
+      ptx::mbar_init(ptx::smem_u32(&sh.stats_rdy[b]), 256);
     }
     for (int i = 0; i < kStages; ++i) {
       ptx::mbar_init(ptx::smem_u32(&sh.kv_full[i]), 1);
       ptx::mbar_init(ptx::smem_u32(&sh.kv_empty[i]), 1);
     }
+    ptx::mbar_init(ptx::smem_u32(&sh.pv_done[0]), 1);
+    ptx::mbar_init(ptx::smem_u32(&sh.pv_done[1]), 1);
+    for (int b = 0; b < 2; ++b)
+      for (int q = 0; q < 4; ++q) ptx::mbar_init(ptx::smem_u32(&sh.xchg[b][q]), 64);
     ptx::mbar_init(ptx::smem_u32(&sh.drain), 1);
     sh.abort_flag = 0;
     ptx::fence_mbar_init();
@@ -646,16 +737,19 @@ __global__ void __launch_bounds__(kThreads, 1)
   ptx::tc_fence_after();
   const uint32_t tmem = sh.tmem_base;
 
-  if (warp < 8) {
+  if (warp >= kSoftmaxWarp0 && warp < kEpiWarp0) {
     ptx::setmaxnreg_inc<kSoftmaxRegs>();
-    softmax_role(sh, p, warp >> 2, tmem);
-  } else {
+    softmax_role(sh, p, (warp - kSoftmaxWarp0) >> 2, tmem);
+  } else if (warp < kSoftmaxWarp0) {
     ptx::setmaxnreg_dec<kControlRegs>();
     if (warp == kLoadWarp) {
-      producer_role(sh, &tq, &tk, &tv, p, lane == 0);
+      if (lane == 0) producer_role(sh, &tq, &tk, &tv, p, true);
     } else if (warp == kMmaWarp) {
-      mma_role(sh, p, tmem, lane == 0);
+      if (lane == 0) mma_role(sh, p, tmem, true);
     }
+  } else {
+    ptx::setmaxnreg_dec<kEpilogueRegs>();
+    epilogue_role(sh, p, tmem);
   }
   __syncwarp();
   ptx::tc_fence_before();
@@ -694,15 +788,18 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-// [rows, 128] fp16 row-major, boxes of 128 rows x 64 columns, 128-byte swizzle.
+// A [rows, 128] fp16 row-major matrix seen as 3-D {64 columns, rows, 2 column halves} with
+// strides {256 B per row, 128 B per half}: one box {64, 128, 2} moves a whole 128x128 tile and
+// lands it as two 16 KB blocks (columns 0..63 of all rows, then 64..127), each in the 128-byte
+// swizzled K-major layout the MMA descriptors address.
 static int make_tile_map(CUtensorMap* map, const void* base, uint64_t rows) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return BSATTN_E_TMA;
-  cuuint64_t dims[2] = {static_cast<cuuint64_t>(kHd), static_cast<cuuint64_t>(rows)};
-  cuuint64_t strides[1] = {static_cast<cuuint64_t>(kHd * 2)};
-  cuuint32_t box[2] = {64, static_cast<cuuint32_t>(kBlk)};
-  cuuint32_t estr[2] = {1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void*>(base), dims, strides,
+  cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), 2};
+  cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHd * 2), 128};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kBlk), 2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BSATTN_OK : BSATTN_E_TMA;
@@ -737,9 +834,7 @@ static int device_setup(int* sms_out) {
     // it assumes; a smaller launch allocation would make setmaxnreg.inc wait forever.
     cudaFuncAttributes fa;
     if (cudaFuncGetAttributes(&fa, bsattn_fwd_kernel) != cudaSuccess) return BSATTN_E_CUDA;
-    if (fa.numRegs < static_cast<int>(kLaunchRegs) ||
-        fa.numRegs * kThreads > 65536)
-      return BSATTN_E_CUDA;
+    if (fa.numRegs != static_cast<int>(kLaunchRegs)) return BSATTN_E_CUDA;
     if (cudaFuncSetAttribute(bsattn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              static_cast<int>(smem_bytes())) != cudaSuccess)
       return BSATTN_E_CUDA;
@@ -828,7 +923,7 @@ int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   p.out_bf16 = out_dtype == BSATTN_OUT_BF16 ? 1 : 0;
   p.timeout_ns = g_timeout_ns;
 
-  const int grid = static_cast<int>(std::min<long long>(sms, (items + 1) / 2));
+  const int grid = static_cast<int>(std::min<long long>(sms, items));
   bsattn_fwd_kernel<<<grid, kThreads, smem_bytes(), static_cast<cudaStream_t>(stream)>>>(tq, tk,
                                                                                         tv, p);
   return cudaGetLastError() == cudaSuccess ? BSATTN_OK : BSATTN_E_CUDA;
