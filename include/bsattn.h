@@ -76,6 +76,28 @@ BSATTN_API int bsattn_fwd(const void* q, const void* k, const void* v, void* o, 
                float scale, int out_dtype,
                void* workspace, size_t workspace_bytes, void* stream);
 
+/* Allocation-free variant of bsattn_fwd.  No counterpart in the reference: its Python entry
+ * point allocated outputs and metadata with torch on every call.
+ *
+ * For callers that cannot allocate device memory where they call attention (for example code
+ * running inside an arena or pool it does not own, or a C caller without a CUDA allocator):
+ * instead of a caller-provided workspace it uses a fixed 256-byte scratch array compiled into
+ * the library, one per GPU, held until the process exits.  It calls no cudaMalloc, cudaFree or
+ * other allocating routine.  The caller still provides q, k, v, o, lse and the CSR arrays, with
+ * the same meaning and limits as bsattn_fwd; the scratch need does not depend on B, H or T, and
+ * a build whose workspace would not fit the array is rejected with BSATTN_E_WORKSPACE.
+ *   - The first call on a device looks up the array's device address (cudaGetSymbolAddress);
+ *     make that first call before capturing `stream` into a CUDA graph.
+ *   - Every call on a device shares the scratch.  Each call clears its error word on `stream`
+ *     before the kernel; calls that overlap on the GPU (different streams) race on it.
+ *   - status (optional, device or pinned host int*): receives 0, BSATTN_E_CSR or
+ *     BSATTN_E_TIMEOUT for this call, written on `stream` after the kernel. */
+BSATTN_API int bsattn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
+                                  const int32_t* row_ptr, const int32_t* col_idx,
+                                  const int32_t* seq_lens, int B, int H, int T, int D,
+                                  int64_t rp_stride_bh, int64_t ci_stride_bh, int max_nnz,
+                                  float scale, int out_dtype, int* status, void* stream);
+
 /* Reads and clears the device error word of `workspace` (synchronises `stream`).
  * *status receives 0, BSATTN_E_CSR or BSATTN_E_TIMEOUT. Replaces the RuntimeError the
  * reference's launcher raised on a failed launch (kernels/v1_baseline.py:126-128). */

@@ -29,6 +29,15 @@ SIGNATURES = {
         _c_void_p, _c_size_t, _c_void_p,          # workspace, bytes, stream
     ]),
     "bsattn_check_error": (_c_int, [_c_void_p, _c_void_p, ctypes.POINTER(_c_int)]),
+    "bsattn_fwd_noalloc": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p,          # q, k, v
+        _c_void_p, _c_void_p,                     # o, lse
+        _c_void_p, _c_void_p, _c_void_p,          # row_ptr, col_idx, seq_lens
+        _c_int, _c_int, _c_int, _c_int,           # B, H, T, D
+        ctypes.c_int64, ctypes.c_int64, _c_int,   # rp_stride_bh, ci_stride_bh, max_nnz
+        ctypes.c_float, _c_int,                   # scale, out_dtype
+        _c_void_p, _c_void_p,                     # status (device or pinned host int*), stream
+    ]),
 }
 
 # error codes (include/bsattn.h)

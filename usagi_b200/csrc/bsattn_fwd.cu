@@ -945,3 +945,65 @@ int bsattn_check_error(void* workspace, void* stream, int* status) {
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free entry point.
+//
+// Some callers cannot allocate device memory at the point they run attention: code executing
+// inside a memory pool or arena they do not own, allocators that are locked or exhausted while
+// a step is in flight, or C callers with no allocator of their own for CUDA memory.  They cannot
+// provide the workspace bsattn_fwd expects, so this entry point supplies it from a fixed array
+// of device memory compiled into the library.  It calls no cudaMalloc, cudaFree or other
+// allocating routine.
+// ------------------------------------------------------------------------------------------
+namespace bsattn {
+
+// Scratch for bsattn_fwd_noalloc: 256 bytes, the whole workspace the kernel uses (its error word
+// plus reserved space).  It does not grow with B, H or T.  Every GPU that loads this library
+// holds one copy until the process exits, and every call on that GPU shares it.
+constexpr size_t kNoAllocScratchBytes = 256;
+static __device__ __align__(256) int g_noalloc_scratch[kNoAllocScratchBytes / sizeof(int)];
+
+// Device address of g_noalloc_scratch per device; host code must not use the symbol itself.
+static void* g_noalloc_addr[64];
+
+static int noalloc_scratch(void** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return BSATTN_E_CUDA;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (g_noalloc_addr[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_noalloc_scratch) != cudaSuccess || ptr == nullptr)
+      return BSATTN_E_CUDA;
+    g_noalloc_addr[dev] = ptr;
+  }
+  *out = g_noalloc_addr[dev];
+  return BSATTN_OK;
+}
+
+}  // namespace bsattn
+
+extern "C" {
+
+int bsattn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
+                       const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens,
+                       int B, int H, int T, int D, int64_t rp_stride_bh, int64_t ci_stride_bh,
+                       int max_nnz, float scale, int out_dtype, int* status, void* stream) {
+  // The workspace the kernel needs must fit the fixed scratch array.
+  if (bsattn_workspace_bytes() > kNoAllocScratchBytes) return BSATTN_E_WORKSPACE;
+  void* scratch = nullptr;
+  int rc = noalloc_scratch(&scratch);
+  if (rc != BSATTN_OK) return rc;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  // The scratch keeps the previous call's contents; the error word must start at zero.
+  if (cudaMemsetAsync(scratch, 0, sizeof(int), s) != cudaSuccess) return BSATTN_E_CUDA;
+  rc = bsattn_fwd(q, k, v, o, lse, row_ptr, col_idx, seq_lens, B, H, T, D, rp_stride_bh,
+                  ci_stride_bh, max_nnz, scale, out_dtype, scratch, kNoAllocScratchBytes, stream);
+  if (rc != BSATTN_OK) return rc;
+  if (status != nullptr &&
+      cudaMemcpyAsync(status, scratch, sizeof(int), cudaMemcpyDefault, s) != cudaSuccess)
+    return BSATTN_E_CUDA;
+  return BSATTN_OK;
+}
+
+}  // extern "C"
