@@ -11,14 +11,15 @@
 //   Query blocks starting at or past seq_len write o = 0, lse = -inf (v4 :63-68).
 //
 // How (B200-native design, not a translation of the Triton program):
-//   * Persistent CTAs, one per SM.  Work items (bh, qb) are dealt round-robin in order of
-//     decreasing qb (longest causal rows first).  Each CTA streams its items' 128x128 tiles
+//   * Persistent CTAs, one per SM.  Work items (bh, qb) are dealt round-robin, in groups of heads
+//     whose K/V fit in L2 and, within a group, in order of decreasing qb (longest rows first).  Each CTA streams its items' 128x128 tiles
 //     through one continuous pipeline: tile t of the CTA uses S buffer t%2, item i uses Q and O
 //     buffers i%2, so the next tile's QK^T and the next item's MMAs overlap the current softmax
 //     and the previous item's epilogue.
 //   * Warp roles (512 threads, four warpgroups; setmaxnreg re-balances the 128 launch registers):
 //       WG0 warp 0        TMA producer: Q per item, K/V tiles named by col_idx into a ring
-//       WG0 warp 1        tcgen05 MMA issuer and TMEM owner (warps 2-3 idle)
+//       WG0 warp 1        tcgen05 P*V issuer and TMEM owner
+//       WG0 warp 2        tcgen05 Q*K^T issuer (warp 3 idle)
 //       WG1 (warps 4-7)   softmax for keys 0..63 of every tile   (thread t owns query row t)
 //       WG2 (warps 8-11)  softmax for keys 64..127 of every tile (same rows; the two halves of a
 //                         row exchange their maxima through shared memory)
@@ -31,9 +32,9 @@
 //       S[b] = Q K^T (fp32) at columns 128 b, b = 0, 1;  O[b] (fp32) at columns 256 + 128 b.
 //       P (fp16, two per column) overwrites S[b]: keys 0..63 at columns +0..31 (written by WG1),
 //       keys 64..127 at +64..95 (WG2); P*V reads A straight from tensor memory.
-//   * MMA order: S(0), S(1), then one back-to-back burst PV(t), S(t+2) for t = 0, 1, ...; the
-//     producer loads tiles in exactly that order (K0, K1, V0, K2, V1, ...), so the ring is
-//     consumed and released in order.
+//   * MMA issue is split: one warp issues every S(t) = Q K(t)^T (after PV(t-2) finished with the
+//     S buffer), another every PV(t); the producer loads tiles in the order K0, K1, V0, K2, V1, ...
+//     that the two warps consume them.
 //   * Lazy rescale: the running row max m is raised only when a block's max exceeds it by more
 //     than kRescaleLog2 (P stays <= 2^8 in fp16); the final o = O/l and lse are exact.
 //   * Every mbarrier wait is bounded (globaltimer); on expiry the CTA raises an abort flag, all
@@ -61,14 +62,14 @@ constexpr int kTileBytes = kBlk * kHd * 2; // 32 KB fp16 tile
 constexpr int kBoxBytes = kTileBytes / 2;  // one TMA box: 128 rows x 64 columns, 128B swizzle
 constexpr int kThreads = 512;              // 4 warpgroups
 constexpr int kLoadWarp = 0;
-constexpr int kMmaWarp = 1;
+constexpr int kMmaWarp = 1;                // P*V issue, TMEM owner
+constexpr int kMmaSWarp = 2;               // Q*K^T issue
 constexpr int kSoftmaxWarp0 = 4;           // warps 4-7: keys 0..63, warps 8-11: keys 64..127
 constexpr int kEpiWarp0 = 12;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 256;            // O[0] column; O[1] at kOCol + 128
 constexpr float kRescaleLog2 = 8.0f;
 constexpr int kPolyEvery = 4;              // every 4th pair of exponentials runs on the FMA pipe
-constexpr int kPrefetchTiles = 4;          // L2 prefetch distance, in tiles past the K loads
 constexpr int kWsInts = 64;                // workspace: int32[64]
 constexpr uint32_t kIdescQK = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescPV = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/true);
@@ -116,6 +117,7 @@ struct FwdParams {
   int max_nnz;
   int BH, H, T, nqb;
   int total_items;
+  int group_heads;  // heads per item group (their K/V stay in L2 while the group is processed)
   float scale_log2;
   int out_bf16;
   unsigned long long timeout_ns;
@@ -126,11 +128,17 @@ struct Item {
   int bh, qb, seq_len, n_steps, row_start;
 };
 
-// Items are numbered band-major with bands in decreasing qb: item g -> qb = nqb-1 - g/BH.
+// Item order: heads are taken in groups of group_heads (sized on the host so a group's K and V fit
+// in L2 with room to spare); inside a group, bands of decreasing qb (longest causal rows first),
+// and inside a band the group's heads.  Item g -> (bh, qb).
 __device__ __forceinline__ Item load_item(const FwdParams& p, int g, bool* csr_bad) {
   Item it;
-  const int band = g / p.BH;
-  it.bh = g - band * p.BH;
+  const int per_group = p.group_heads * p.nqb;
+  const int grp = g / per_group;
+  const int r = g - grp * per_group;
+  const int gh = min(p.group_heads, p.BH - grp * p.group_heads);
+  const int band = r / gh;
+  it.bh = grp * p.group_heads + (r - band * gh);
   it.qb = p.nqb - 1 - band;
   int sl = p.T;
   if (p.seq_lens != nullptr) sl = min(__ldg(p.seq_lens + it.bh / p.H), p.T);
@@ -317,23 +325,6 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
     }
     return kb;
   };
-  // pf runs kPrefetchTiles ahead of ks and pulls each tile's K, V (and Q at an item start)
-  // into L2, so the shared-memory loads that follow hit L2 instead of HBM.
-  TileIter pf;
-  tile_begin(pf, p, nullptr);
-  auto prefetch = [&]() {
-    if (!pf.valid) return;
-    if (leader) {
-      const int head_row0 = pf.it.bh * p.T;
-      if (pf.j == 0) ptx::tma_prefetch_l2_3d(tq, 0, head_row0 + pf.it.qb * kBlk, 0);
-      const int row = head_row0 + key_block(pf) * kBlk;
-      ptx::tma_prefetch_l2_3d(tk, 0, row, 0);
-      ptx::tma_prefetch_l2_3d(tv, 0, row, 0);
-    }
-    tile_next(pf, p, nullptr);
-  };
-  for (int i = 0; i < kPrefetchTiles + 2; ++i) prefetch();
-
   tile_begin(ks, p, &csr_bad);
   tile_begin(vs, p, nullptr);
   for (int i = 0; i < 2 && ok && ks.valid; ++i) {
@@ -347,7 +338,6 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
       ok = load_K(ks);
       tile_next(ks, p, &csr_bad);
     }
-    prefetch();
     tile_next(vs, p, nullptr);
   }
   if (csr_bad && leader) raise_error(p, BSATTN_E_CSR);
@@ -362,109 +352,96 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
 }
 
 // ------------------------------------------------------------------------------------------
-// MMA warp: S(0), S(1), then per tile one burst "PV(t), S(t+2)".  tcgen05.mma issue blocks at the
-// tensor pipe's execution rate (its queue holds only a couple of instructions), so the pipe
-// drains whenever this warp pauses; every wait for a burst is therefore done before its first
-// MMA, and the sixteen MMAs then go out back to back.  The whole warp runs the schedule and builds
-// the descriptors (warp-uniform values); lane 0 issues every tcgen05.mma and tcgen05.commit, so
-// one thread owns all MMA completions.  Descriptors are advanced by adding (byte offset >> 4) to
-// the start-address field, which never carries out of its 14 bits inside 227 KB of shared memory.
+// MMA issue, split over two warps so that one warp's barrier waits overlap the other's MMAs
+// (tcgen05.mma issue blocks at the tensor pipe's rate; its queue holds only a couple of MMAs):
+//   warp kMmaWarp   (PV)  waits V(t) and both halves of P(t), issues O[ii%2] (+)= P(t) V(t)
+//   warp kMmaSWarp  (S)   waits Q, K(t) and "PV(t-2) done", issues S[t%2] = Q K(t)^T
+// S(t) overwrites the S buffer that held P(t-2), hence the wait on pv_done before it.  Each role
+// runs on lane 0 and commits its own MMAs.  Ring positions follow the producer's load order
+// K0, K1, V0, K2, V1, K3, ...: K(t) sits at position t for t < 2 and 2t-1 after; V(t) at 2t+2,
+// except for the CTA's last tile, whose V follows V(t-1) directly (no K(t+1) exists) at 2t+1.  Descriptors are
+// advanced by adding (byte offset >> 4) to the start-address field, which never carries out of
+// its 14 bits inside 227 KB of shared memory.
 // ------------------------------------------------------------------------------------------
-__device__ void mma_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem, bool leader) {
-  TileIter ss, pv;  // ss runs two tiles ahead of pv
-  int stage = 0;
-  uint32_t kv_phase = 0;
+__device__ __forceinline__ void ring_slot(int pos, int& stage, uint32_t& phase) {
+  stage = pos % kStages;
+  phase = static_cast<uint32_t>(pos / kStages) & 1u;
+}
+
+__device__ void mma_s_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem) {
   const uint64_t q_desc0 = ptx::sdesc_sw128(ptx::smem_u32(sh.q[0]), 16, 1024);
   const uint64_t k_desc0 = ptx::sdesc_sw128(ptx::smem_u32(sh.kv[0]), 16, 1024);
+  const uint32_t kv_full0 = ptx::smem_u32(&sh.kv_full[0]);
+  const uint32_t kv_empty0 = ptx::smem_u32(&sh.kv_empty[0]);
+  TileIter x;
+  tile_begin(x, p, nullptr);
+  while (x.valid) {
+    const int qb = x.ii & 1;
+    const int sb = x.t & 1;
+    int stage;
+    uint32_t phase;
+    ring_slot(x.t < 2 ? x.t : 2 * x.t - 1, stage, phase);
+    if (x.j == 0 &&
+        !wait_ctl(ptx::smem_u32(&sh.q_full[qb]), (static_cast<uint32_t>(x.ii) >> 1) & 1u, sh, p))
+      return;
+    if (!wait_ctl(kv_full0 + stage * 8, phase, sh, p)) return;
+    if (x.t >= 2 &&  // PV(t-2) has read the P stored in S[sb]
+        !wait_ctl(ptx::smem_u32(&sh.pv_done[sb]), (static_cast<uint32_t>(x.t - 2) >> 1) & 1u, sh, p))
+      return;
+    ptx::tc_fence_after();
+    const uint64_t qd = q_desc0 + static_cast<uint32_t>((qb * kTileBytes) >> 4);
+    const uint64_t kd = k_desc0 + static_cast<uint32_t>((stage * kTileBytes) >> 4);
+    const uint32_t d = tmem + sb * 128;
+#pragma unroll
+    for (int kk = 0; kk < kHd / 16; ++kk) {
+      const uint32_t off = ((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4;
+      ptx::mma_ss(d, qd + off, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
+    }
+    ptx::tc_commit(kv_empty0 + stage * 8);
+    ptx::tc_commit(ptx::smem_u32(&sh.s_full[sb]));
+    if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.q_empty[qb]));
+    tile_next(x, p, nullptr);
+  }
+}
+
+__device__ void mma_pv_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem) {
   const uint64_t v_desc0 = ptx::sdesc_sw128(ptx::smem_u32(sh.kv[0]), kBoxBytes, 1024);
   const uint32_t kv_full0 = ptx::smem_u32(&sh.kv_full[0]);
   const uint32_t kv_empty0 = ptx::smem_u32(&sh.kv_empty[0]);
-  bool ok = true;
-
-  // Waits that must precede S(x): its Q (first tile of an item) and its K tile at `kstage`.
-  auto wait_S = [&](const TileIter& x, int kstage, uint32_t kphase) -> bool {
-    if (x.j == 0 &&
-        !wait_ctl(ptx::smem_u32(&sh.q_full[x.ii & 1]), (static_cast<uint32_t>(x.ii) >> 1) & 1u, sh, p))
-      return false;
-    return wait_ctl(kv_full0 + kstage * 8, kphase, sh, p);
-  };
-  auto issue_S = [&](const TileIter& x, int kstage) {
-    const int qb = x.ii & 1;
+  TileIter x, nx;  // nx = the tile after x (tells whether x is the CTA's last tile)
+  tile_begin(x, p, nullptr);
+  nx = x;
+  if (nx.valid) tile_next(nx, p, nullptr);
+  while (x.valid) {
+    const int ob = x.ii & 1;
     const int sb = x.t & 1;
-    const uint64_t qd = q_desc0 + static_cast<uint32_t>((qb * kTileBytes) >> 4);
-    const uint64_t kd = k_desc0 + static_cast<uint32_t>((kstage * kTileBytes) >> 4);
-    const uint32_t d = tmem + sb * 128;
-    if (leader) {
-#pragma unroll
-      for (int kk = 0; kk < kHd / 16; ++kk) {
-        const uint32_t off = ((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4;
-        ptx::mma_ss(d, qd + off, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
-      }
-      ptx::tc_commit(kv_empty0 + kstage * 8);
-      ptx::tc_commit(ptx::smem_u32(&sh.s_full[sb]));
-      if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.q_empty[qb]));
-    }
-  };
-  auto advance = [&](int& st, uint32_t& ph) {
-    if (++st == kStages) st = 0, ph ^= 1u;
-  };
-
-  tile_begin(ss, p, nullptr);
-  tile_begin(pv, p, nullptr);
-  for (int i = 0; i < 2 && ok && ss.valid; ++i) {
-    ok = wait_S(ss, stage, kv_phase);
-    if (!ok) break;
+    const uint32_t tph = (static_cast<uint32_t>(x.t) >> 1) & 1u;
+    int stage;
+    uint32_t phase;
+    ring_slot(nx.valid ? 2 * x.t + 2 : 2 * x.t + 1, stage, phase);
+    if (!wait_ctl(kv_full0 + stage * 8, phase, sh, p)) return;
+    if (x.j == 0 && x.ii >= 2 &&  // O[ob] read out by the epilogue of item ii-2
+        !wait_ctl(ptx::smem_u32(&sh.o_free[ob]), ((static_cast<uint32_t>(x.ii) >> 1) + 1u) & 1u, sh, p))
+      return;
+    if (!wait_ctl(ptx::smem_u32(&sh.p_rdy[sb][0]), tph, sh, p)) return;
+    if (!wait_ctl(ptx::smem_u32(&sh.p_rdy[sb][1]), tph, sh, p)) return;
     ptx::tc_fence_after();
-    issue_S(ss, stage);
-    advance(stage, kv_phase);
-    tile_next(ss, p, nullptr);
-  }
-  while (ok && pv.valid) {
-    // ---- every wait of the burst first
-    const int vstage = stage;
-    const uint32_t vphase = kv_phase;
-    int kstage = vstage;
-    uint32_t kphase = vphase;
-    advance(kstage, kphase);
-    const int ob = pv.ii & 1;
-    const int sb = pv.t & 1;
-    const uint32_t tph = (static_cast<uint32_t>(pv.t) >> 1) & 1u;
-    ok = wait_ctl(kv_full0 + vstage * 8, vphase, sh, p);
-    if (ok && pv.j == 0 && pv.ii >= 2)  // O[ob] read out by the epilogue of item ii-2
-      ok = wait_ctl(ptx::smem_u32(&sh.o_free[ob]), ((static_cast<uint32_t>(pv.ii) >> 1) + 1u) & 1u,
-                     sh, p);
-    if (ok) ok = wait_ctl(ptx::smem_u32(&sh.p_rdy[sb][0]), tph, sh, p);
-    if (ok) ok = wait_ctl(ptx::smem_u32(&sh.p_rdy[sb][1]), tph, sh, p);
-    if (ok && ss.valid) ok = wait_S(ss, kstage, kphase);
-    if (!ok) break;
-    ptx::tc_fence_after();
-    // ---- PV(t): O[ob] (+)= P(t) V(t)
-    const uint64_t vd = v_desc0 + static_cast<uint32_t>((vstage * kTileBytes) >> 4);
+    const uint64_t vd = v_desc0 + static_cast<uint32_t>((stage * kTileBytes) >> 4);
     const uint32_t d = tmem + kOCol + ob * 128;
     const uint32_t a = tmem + sb * 128;
-    if (leader) {
 #pragma unroll
-      for (int kk = 0; kk < kBlk / 16; ++kk) {
-        // V is [key][d] with d contiguous: MN-major B operand.  One K step = 16 keys = two
-        // 8-row swizzle atoms (2 KB); the second 64-column half of d sits one TMA box later.
-        // P keys 0..63 sit at columns +0..31 of S[sb], keys 64..127 at +64..95.
-        ptx::mma_ts(d, a + (kk >> 2) * 64 + (kk & 3) * 8,
-                    vd + static_cast<uint32_t>((kk * 2048) >> 4), kIdescPV,
-                    (pv.j > 0 || kk > 0) ? 1u : 0u);
-      }
-      ptx::tc_commit(kv_empty0 + vstage * 8);
-      ptx::tc_commit(ptx::smem_u32(&sh.pv_done[sb]));
-      if (pv.j == pv.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.o_full[ob]));
+    for (int kk = 0; kk < kBlk / 16; ++kk) {
+      // V is [key][d] with d contiguous: MN-major B operand.  One K step = 16 keys = two 8-row
+      // swizzle atoms (2 KB); the second 64-column half of d sits one TMA box later.  P keys
+      // 0..63 sit at columns +0..31 of S[sb], keys 64..127 at +64..95.
+      ptx::mma_ts(d, a + (kk >> 2) * 64 + (kk & 3) * 8, vd + static_cast<uint32_t>((kk * 2048) >> 4),
+                  kIdescPV, (x.j > 0 || kk > 0) ? 1u : 0u);
     }
-    // ---- S(t+2) straight after, into the S buffer PV(t) just read
-    if (ss.valid) issue_S(ss, kstage);
-    stage = kstage;
-    kv_phase = kphase;
-    if (ss.valid) {
-      advance(stage, kv_phase);
-      tile_next(ss, p, nullptr);
-    }
-    tile_next(pv, p, nullptr);
+    ptx::tc_commit(kv_empty0 + stage * 8);
+    ptx::tc_commit(ptx::smem_u32(&sh.pv_done[sb]));
+    if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.o_full[ob]));
+    x = nx;
+    if (nx.valid) tile_next(nx, p, nullptr);
   }
 }
 
@@ -719,7 +696,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(ptx::smem_u32(&sh.pv_done[1]), 1);
     for (int b = 0; b < 2; ++b)
       for (int q = 0; q < 4; ++q) ptx::mbar_init(ptx::smem_u32(&sh.xchg[b][q]), 64);
-    ptx::mbar_init(ptx::smem_u32(&sh.drain), 1);
+    ptx::mbar_init(ptx::smem_u32(&sh.drain), 2);  // one commit per MMA-issuing thread
     sh.abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -745,7 +722,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (warp == kLoadWarp) {
       if (lane == 0) producer_role(sh, &tq, &tk, &tv, p, true);
     } else if (warp == kMmaWarp) {
-      if (lane == 0) mma_role(sh, p, tmem, true);
+      if (lane == 0) mma_pv_role(sh, p, tmem);
+    } else if (warp == kMmaSWarp) {
+      if (lane == 0) mma_s_role(sh, p, tmem);
     }
   } else {
     ptx::setmaxnreg_dec<kEpilogueRegs>();
@@ -754,12 +733,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncwarp();
   ptx::tc_fence_before();
   __syncthreads();
+  // Each MMA-issuing thread commits once more; when both commits have arrived, every MMA of the
+  // CTA has completed and the tensor memory can be released.
+  if ((warp == kMmaWarp || warp == kMmaSWarp) && lane == 0)
+    ptx::tc_commit(ptx::smem_u32(&sh.drain));
   if (warp == kMmaWarp) {
-    if (lane == 0) {
-      // Every MMA this thread issued has completed once this commit arrives.
-      ptx::tc_commit(ptx::smem_u32(&sh.drain));
-      wait_drain(ptx::smem_u32(&sh.drain), 0, p);
-    }
+    if (lane == 0) wait_drain(ptx::smem_u32(&sh.drain), 0, p);
     __syncwarp();
     ptx::tc_fence_after();
     ptx::tmem_dealloc(tmem, kTmemCols);
@@ -918,6 +897,10 @@ int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   p.T = T;
   p.nqb = T / kBlk;
   p.total_items = static_cast<int>(items);
+  // K and V of one head take 2 * T * 128 * 2 bytes; keep a group's worth near 32 MB of L2.
+  const long long head_kv_bytes = 512ll * T;
+  p.group_heads = static_cast<int>(
+      std::max<long long>(1, std::min<long long>(B * H, (32ll << 20) / head_kv_bytes)));
   const double sc = scale > 0.0f ? static_cast<double>(scale) : 1.0 / sqrt(static_cast<double>(D));
   p.scale_log2 = static_cast<float>(sc * 1.4426950408889634);
   p.out_bf16 = out_dtype == BSATTN_OUT_BF16 ? 1 : 0;

@@ -95,13 +95,6 @@ __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint
       : "memory");
 }
 
-// Bring a tile into L2 ahead of its load; no shared memory or barrier involved.
-__device__ __forceinline__ void tma_prefetch_l2_3d(const void* tmap, int x, int y, int z) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(tmap),
-               "r"(x), "r"(y), "r"(z)
-               : "memory");
-}
-
 __device__ __forceinline__ uint64_t policy_evict_last() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
