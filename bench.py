@@ -323,7 +323,20 @@ def main():
     if os.environ.get("NCCL_DEBUG", "").upper() == "VERSION":
         os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the single JSON line
     if world > 1:
-        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+        # NCCL announces itself on stdout when the communicator is created; send that to stderr so
+        # stdout carries only the JSON line.
+        sys.stdout.flush()
+        saved_fd = os.dup(1)
+        os.dup2(2, 1)
+        try:
+            dist.init_process_group("nccl", device_id=device,
+                                    timeout=datetime.timedelta(seconds=120))
+            dist.barrier()
+            torch.cuda.synchronize()
+        finally:
+            sys.stdout.flush()
+            os.dup2(saved_fd, 1)
+            os.close(saved_fd)
     ub.setup(device=str(device))
 
     peaks = load_peaks()
