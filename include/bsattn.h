@@ -112,6 +112,12 @@ BSATTN_API int bsattn_setup(void);
  * BSATTN_E_TIMEOUT through bsattn_check_error. Applies to later launches in this process. */
 BSATTN_API void bsattn_set_timeout_ns(uint64_t ns);
 
+/* Test hook (no counterpart in the reference): while enabled, later launches make their
+ * QK^T-issuing thread first wait on a barrier that nothing signals, so that the wait runs
+ * into the bsattn_set_timeout_ns bound and the launch ends with BSATTN_E_TIMEOUT. Used to
+ * test the timeout path on a GPU without faulting it. Off by default. */
+BSATTN_API void bsattn_test_unsignalled_wait(int enable);
+
 /* Human-readable text for a BSATTN_E* code. */
 BSATTN_API const char* bsattn_strerror(int code);
 

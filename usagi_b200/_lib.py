@@ -17,6 +17,7 @@ SIGNATURES = {
     "bsattn_workspace_bytes": (_c_size_t, []),
     "bsattn_version": (_c_int, []),
     "bsattn_set_timeout_ns": (None, [ctypes.c_uint64]),
+    "bsattn_test_unsignalled_wait": (None, [_c_int]),
     "bsattn_setup": (_c_int, []),
     "bsattn_strerror": (ctypes.c_char_p, [_c_int]),
     "bsattn_fwd": (_c_int, [

@@ -70,6 +70,9 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kOCol = 256;            // O[0] column; O[1] at kOCol + 128
 constexpr float kRescaleLog2 = 8.0f;
 constexpr int kPolyEvery = 4;              // every 4th pair of exponentials runs on the FMA pipe
+// Lower bound for the teardown waits on in-flight copies and MMAs, whatever timeout_ns is: they
+// finish within microseconds, and the CTA must not exit (or free tensor memory) before they do.
+constexpr unsigned long long kDrainNs = 100000000ull;
 constexpr int kWsInts = 64;                // workspace: int32[64]
 constexpr uint32_t kIdescQK = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescPV = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/true);
@@ -101,6 +104,7 @@ struct alignas(1024) SharedStorage {
   uint64_t o_free[2];         // epilogue done reading O[b] and its stats
   uint64_t stats_rdy[2];      // softmax published stats[b]
   uint64_t drain;
+  uint64_t unsignalled;       // never arrived on; waited on only by the test hook
   uint32_t tmem_base;
   int abort_flag;
 };
@@ -121,6 +125,7 @@ struct FwdParams {
   float scale_log2;
   int out_bf16;
   unsigned long long timeout_ns;
+  int test_unsignalled_wait;  // test hook: the QK^T issuer first waits on a barrier nobody signals
 };
 
 // One work item = one (head, query block).
@@ -240,11 +245,13 @@ __device__ __forceinline__ bool wait_ctl(uint32_t bar, uint32_t parity, SharedSt
 }
 
 // Drain wait used during teardown: ignores the abort flag, still bounded in time.
+// Its bound is at least kDrainNs, so a very short pipeline timeout cannot cut the drain short.
 __device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity, const FwdParams& p) {
+  const uint64_t bound = p.timeout_ns > kDrainNs ? p.timeout_ns : kDrainNs;
   const uint64_t t0 = ptx::globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (ptx::mbar_try_wait(bar, parity)) return;
-    if ((it & 63u) == 0 && ptx::globaltimer_ns() - t0 > p.timeout_ns) {
+    if ((it & 63u) == 0 && ptx::globaltimer_ns() - t0 > bound) {
       raise_error(p, BSATTN_E_TIMEOUT);
       return;
     }
@@ -341,14 +348,14 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
     tile_next(vs, p, nullptr);
   }
   if (csr_bad && leader) raise_error(p, BSATTN_E_CSR);
-  if (!ok) {
-    // Aborted: make sure no TMA write is still landing in shared memory before the CTA exits.
-    for (int i = 0; i < kStages; ++i)
-      if ((kv_issued >> i) & 1u) wait_drain(kv_full0 + i * 8, (kv_last_parity >> i) & 1u, p);
-    for (int b = 0; b < 2; ++b)
-      if ((q_issued >> b) & 1u)
-        wait_drain(ptx::smem_u32(&sh.q_full[b]), (q_last_parity >> b) & 1u, p);
-  }
+  // No TMA write may still be landing in shared memory when the CTA exits.  On a normal run every
+  // copy was consumed and these waits return at once; after an abort (here or in another role)
+  // the last copies may still be in flight.
+  for (int i = 0; i < kStages; ++i)
+    if ((kv_issued >> i) & 1u) wait_drain(kv_full0 + i * 8, (kv_last_parity >> i) & 1u, p);
+  for (int b = 0; b < 2; ++b)
+    if ((q_issued >> b) & 1u)
+      wait_drain(ptx::smem_u32(&sh.q_full[b]), (q_last_parity >> b) & 1u, p);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -373,6 +380,8 @@ __device__ void mma_s_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem)
   const uint64_t k_desc0 = ptx::sdesc_sw128(ptx::smem_u32(sh.kv[0]), 16, 1024);
   const uint32_t kv_full0 = ptx::smem_u32(&sh.kv_full[0]);
   const uint32_t kv_empty0 = ptx::smem_u32(&sh.kv_empty[0]);
+  // Test hook for the timeout path: a wait that can only end by running out of time.
+  if (p.test_unsignalled_wait && !wait_ctl(ptx::smem_u32(&sh.unsignalled), 0, sh, p)) return;
   TileIter x;
   tile_begin(x, p, nullptr);
   while (x.valid) {
@@ -697,6 +706,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int b = 0; b < 2; ++b)
       for (int q = 0; q < 4; ++q) ptx::mbar_init(ptx::smem_u32(&sh.xchg[b][q]), 64);
     ptx::mbar_init(ptx::smem_u32(&sh.drain), 2);  // one commit per MMA-issuing thread
+    ptx::mbar_init(ptx::smem_u32(&sh.unsignalled), 1);
     sh.abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -731,6 +741,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     epilogue_role(sh, p, tmem);
   }
   __syncwarp();
+  // A role that aborted may have left a tensor-memory load or store of its own in flight.
+  ptx::tmem_wait_ld();
+  ptx::tmem_wait_st();
   ptx::tc_fence_before();
   __syncthreads();
   // Each MMA-issuing thread commits once more; when both commits have arrived, every MMA of the
@@ -793,6 +806,7 @@ struct DeviceInfo {
 static std::mutex g_mu;
 static DeviceInfo g_dev[64];
 static unsigned long long g_timeout_ns = 2000000000ull;
+static int g_test_unsignalled_wait = 0;
 
 static size_t smem_bytes() { return sizeof(SharedStorage) + 1024; }
 
@@ -836,6 +850,8 @@ size_t bsattn_workspace_bytes(void) { return kWsInts * sizeof(int); }
 int bsattn_version(void) { return 100; }
 
 void bsattn_set_timeout_ns(uint64_t ns) { g_timeout_ns = ns > 0 ? ns : 1; }
+
+void bsattn_test_unsignalled_wait(int enable) { g_test_unsignalled_wait = enable ? 1 : 0; }
 
 int bsattn_setup(void) { return device_setup(nullptr); }
 
@@ -905,6 +921,7 @@ int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   p.scale_log2 = static_cast<float>(sc * 1.4426950408889634);
   p.out_bf16 = out_dtype == BSATTN_OUT_BF16 ? 1 : 0;
   p.timeout_ns = g_timeout_ns;
+  p.test_unsignalled_wait = g_test_unsignalled_wait;
 
   const int grid = static_cast<int>(std::min<long long>(sms, items));
   bsattn_fwd_kernel<<<grid, kThreads, smem_bytes(), static_cast<cudaStream_t>(stream)>>>(tq, tk,
