@@ -58,8 +58,12 @@ enum {
   BSATTN_E_DTYPE = -10      /* unsupported dtype code                                       */
 };
 
-/* Output element type of `o`. */
-enum { BSATTN_OUT_F16 = 0, BSATTN_OUT_BF16 = 1 };
+/* dtype_flags of bsattn_fwd: element types of the inputs and of `o`, OR-ed together.
+ *   BSATTN_OUT_F16 / BSATTN_OUT_BF16: o is fp16 / bf16 (the reference stored bf16, v4 :132, :152).
+ *   BSATTN_IN_BF16: q and k are bf16 (the reference's input type, v4 :215); v is fp16 either way,
+ *     because the reference multiplies fp16(P) by fp16(V) (v4 :103, :123) and one tensor-core MMA
+ *     takes both operands in the same type.  bsattn_bf16_to_f16 converts a bf16 V. */
+enum { BSATTN_OUT_F16 = 0, BSATTN_OUT_BF16 = 1, BSATTN_IN_BF16 = 2 };
 
 /* Bytes of device workspace bsattn_fwd needs (error word, scheduler state). Zero it once
  * before first use (cudaMemset); the kernel leaves it ready for the next call. One workspace
@@ -73,7 +77,7 @@ BSATTN_API int bsattn_fwd(const void* q, const void* k, const void* v, void* o, 
                const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens,
                int B, int H, int T, int D,
                int64_t rp_stride_bh, int64_t ci_stride_bh, int max_nnz,
-               float scale, int out_dtype,
+               float scale, int dtype_flags,
                void* workspace, size_t workspace_bytes, void* stream);
 
 /* Allocation-free variant of bsattn_fwd.  No counterpart in the reference: its Python entry
@@ -96,7 +100,7 @@ BSATTN_API int bsattn_fwd_noalloc(const void* q, const void* k, const void* v, v
                                   const int32_t* row_ptr, const int32_t* col_idx,
                                   const int32_t* seq_lens, int B, int H, int T, int D,
                                   int64_t rp_stride_bh, int64_t ci_stride_bh, int max_nnz,
-                                  float scale, int out_dtype, int* status, void* stream);
+                                  float scale, int dtype_flags, int* status, void* stream);
 
 /* Reads and clears the device error word of `workspace` (synchronises `stream`).
  * *status receives 0, BSATTN_E_CSR or BSATTN_E_TIMEOUT. Replaces the RuntimeError the
@@ -117,6 +121,11 @@ BSATTN_API void bsattn_set_timeout_ns(uint64_t ns);
  * into the bsattn_set_timeout_ns bound and the launch ends with BSATTN_E_TIMEOUT. Used to
  * test the timeout path on a GPU without faulting it. Off by default. */
 BSATTN_API void bsattn_test_unsignalled_wait(int enable);
+
+/* Converts n bf16 values at src to fp16 at dst (round to nearest even; exact for values inside
+ * the fp16 range) on `stream`: the v.to(tl.float16) of the reference's P V product (v4 :103, :123)
+ * done once per call instead of per tile.  n % 8 == 0; src and dst 16-byte aligned. */
+BSATTN_API int bsattn_bf16_to_f16(const void* src, void* dst, int64_t n, void* stream);
 
 /* Human-readable text for a BSATTN_E* code. */
 BSATTN_API const char* bsattn_strerror(int code);

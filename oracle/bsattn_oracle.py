@@ -198,9 +198,11 @@ def attn_online_literal(q, k, v, row_ptr, col_idx, seq_lens=None):
     B, H, T, D, BH, nqb, rp, ci, sl = _flat_meta(q, row_ptr, col_idx, seq_lens)
     qk_scale = np.float32((1.0 / math.sqrt(D)) * math.log2(math.e))
     ln2 = np.float32(math.log(2.0))
-    qn = q.reshape(BH, T, D).cpu().numpy()
-    kn = k.reshape(BH, T, D).cpu().numpy()
-    vn = v.reshape(BH, T, D).cpu().numpy()
+    # fp16 and bf16 values are exact in fp32.  V goes through fp16 below whatever its input type:
+    # the reference multiplies fp16(P) by v.to(tl.float16) (v4 :103, :123).
+    qn = q.reshape(BH, T, D).float().cpu().numpy()
+    kn = k.reshape(BH, T, D).float().cpu().numpy()
+    vn = v.reshape(BH, T, D).float().cpu().numpy()
     o = np.zeros((BH, T, D), np.float32)
     lse = np.full((BH, T), -np.inf, np.float32)
     offs = np.arange(BLOCK)

@@ -65,9 +65,29 @@ def test_argument_validation_before_device():
     assert _call(B=0) == _lib.E_SHAPE
     assert _call(nnz=-1) == _lib.E_SHAPE
     assert _call(od=7) == _lib.E_DTYPE
+    assert _call(od=4) == _lib.E_DTYPE
     assert _call(q=24) == _lib.E_ALIGN
     assert _call(ws=None) == _lib.E_WORKSPACE
     assert _call(wsb=4) == _lib.E_WORKSPACE
+
+
+def test_bf16_converter_validation_before_device():
+    lib = _lib.load()
+    assert lib.bsattn_bf16_to_f16(None, 16, 8, None) == _lib.E_NULL
+    assert lib.bsattn_bf16_to_f16(16, 32, 12, None) == _lib.E_SHAPE
+    assert lib.bsattn_bf16_to_f16(16, 32, -8, None) == _lib.E_SHAPE
+    assert lib.bsattn_bf16_to_f16(24, 32, 8, None) == _lib.E_ALIGN
+    assert lib.bsattn_bf16_to_f16(16, 32, 0, None) == _lib.OK
+
+
+def test_python_api_dtype_rules():
+    q = torch.zeros(1, 1, 128, 128, dtype=torch.float16)
+    rp = torch.tensor([0, 1], dtype=torch.int32)
+    ci = torch.tensor([0], dtype=torch.int32)
+    for qq, kk, vv in ((q.bfloat16(), q, q), (q.float(), q.float(), q.float()),
+                       (q, q, q.bfloat16())):
+        with pytest.raises(TypeError):
+            api.block_sparse_attn_fwd(qq, kk, vv, rp, ci)
 
 
 def test_python_api_refuses_cpu_tensors():

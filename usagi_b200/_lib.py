@@ -26,17 +26,18 @@ SIGNATURES = {
         _c_void_p, _c_void_p, _c_void_p,          # row_ptr, col_idx, seq_lens
         _c_int, _c_int, _c_int, _c_int,           # B, H, T, D
         ctypes.c_int64, ctypes.c_int64, _c_int,   # rp_stride_bh, ci_stride_bh, max_nnz
-        ctypes.c_float, _c_int,                   # scale, out_dtype
+        ctypes.c_float, _c_int,                   # scale, dtype_flags
         _c_void_p, _c_size_t, _c_void_p,          # workspace, bytes, stream
     ]),
     "bsattn_check_error": (_c_int, [_c_void_p, _c_void_p, ctypes.POINTER(_c_int)]),
+    "bsattn_bf16_to_f16": (_c_int, [_c_void_p, _c_void_p, ctypes.c_int64, _c_void_p]),
     "bsattn_fwd_noalloc": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p,          # q, k, v
         _c_void_p, _c_void_p,                     # o, lse
         _c_void_p, _c_void_p, _c_void_p,          # row_ptr, col_idx, seq_lens
         _c_int, _c_int, _c_int, _c_int,           # B, H, T, D
         ctypes.c_int64, ctypes.c_int64, _c_int,   # rp_stride_bh, ci_stride_bh, max_nnz
-        ctypes.c_float, _c_int,                   # scale, out_dtype
+        ctypes.c_float, _c_int,                   # scale, dtype_flags
         _c_void_p, _c_void_p,                     # status (device or pinned host int*), stream
     ]),
 }
@@ -45,7 +46,7 @@ SIGNATURES = {
 OK = 0
 E_SHAPE, E_ALIGN, E_NULL, E_WORKSPACE, E_CUDA, E_TMA, E_DEVICE, E_CSR, E_TIMEOUT, E_DTYPE = (
     -1, -2, -3, -4, -5, -6, -7, -8, -9, -10)
-OUT_F16, OUT_BF16 = 0, 1
+OUT_F16, OUT_BF16, IN_BF16 = 0, 1, 2
 
 _lock = threading.Lock()
 _lib = None

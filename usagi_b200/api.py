@@ -10,8 +10,10 @@ Reference interface (sissississi-013/usagi, kernels/v4_leaderboard_0740ms.py):
 
 Differences a caller can see, all deliberate:
 
-* ``o`` is fp16 by default (the reference stored bf16, v4 :152); pass ``out_dtype=torch.bfloat16``
-  for the reference's output dtype.
+* ``o`` has the dtype of ``q`` by default: bf16 for the reference's bf16 inputs (v4 :152), fp16
+  for fp16 inputs (the reference always stored bf16); ``out_dtype`` overrides it.
+* bf16 inputs follow the reference's mixed recipe: Q K^T on bf16 operands, then fp16(P) times
+  fp16(V) (v4 :103, :123).  A bf16 ``v`` is converted to fp16 once per call, by the library.
 * No metadata cache keyed on ``data_ptr()`` (the reference's v4 :155-164 cache returns stale
   metadata when a freed buffer is reused with new content); int32 conversions happen per call and
   are no-ops for int32 inputs.
@@ -121,16 +123,17 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                           row_ptr: torch.Tensor, col_idx: torch.Tensor,
                           seq_lens: Optional[torch.Tensor] = None, *,
                           scale: Optional[float] = None,
-                          out_dtype: torch.dtype = torch.float16,
+                          out_dtype: Optional[torch.dtype] = None,
                           out: Optional[torch.Tensor] = None,
                           lse_out: Optional[torch.Tensor] = None,
                           return_lse: bool = True):
     """Block-sparse causal attention forward on a B200.
 
-    q, k, v: fp16 [B, H, T, 128] CUDA tensors, T % 128 == 0.
-    row_ptr: int [B, H, T/128 + 1]; col_idx: int [B, H, max_nnz] (or [B*H, .], or one shared
-    [.] row); seq_lens: int [B] or None.  Returns ``(o, lse)`` like the reference (v4 :179):
-    o [B, H, T, 128] in ``out_dtype``, lse fp32 [B, H, T] (None if ``return_lse=False``).
+    q, k: fp16 or bf16 [B, H, T, 128] CUDA tensors of one dtype, T % 128 == 0; v: the same shape,
+    fp16 or the dtype of q.  row_ptr: int [B, H, T/128 + 1]; col_idx: int [B, H, max_nnz] (or
+    [B*H, .], or one shared [.] row); seq_lens: int [B] or None.  Returns ``(o, lse)`` like the
+    reference (v4 :179): o [B, H, T, 128] in ``out_dtype`` (default: q's dtype), lse fp32
+    [B, H, T] (None if ``return_lse=False``).
     """
     lib = _lib.load()
     if q.dim() != 4:
@@ -138,14 +141,29 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     B, H, T, D = q.shape
     if k.shape != q.shape or v.shape != q.shape:
         raise ValueError("q, k, v must have the same shape")
+    if q.dtype not in (torch.float16, torch.bfloat16) or k.dtype != q.dtype \
+            or v.dtype not in (torch.float16, q.dtype):
+        raise TypeError("q and k must both be float16 or both bfloat16, and v float16 or the "
+                        f"dtype of q (got {q.dtype}, {k.dtype}, {v.dtype})")
     if not q.is_cuda:
         raise ValueError("block_sparse_attn_fwd needs CUDA tensors (there is no CPU path)")
-    if q.dtype != torch.float16 or k.dtype != torch.float16 or v.dtype != torch.float16:
-        raise TypeError(f"q, k, v must be float16 (got {q.dtype}, {k.dtype}, {v.dtype})")
+    if out_dtype is None:
+        out_dtype = q.dtype
     if out_dtype not in (torch.float16, torch.bfloat16):
         raise TypeError(f"out_dtype must be float16 or bfloat16, got {out_dtype}")
     dev = q.device
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    flags = _lib.OUT_BF16 if out_dtype == torch.bfloat16 else _lib.OUT_F16
+    if q.dtype == torch.bfloat16:
+        flags |= _lib.IN_BF16
+    if v.dtype == torch.bfloat16:
+        v16 = torch.empty(v.shape, device=dev, dtype=torch.float16)
+        with torch.cuda.device(dev):
+            rc = lib.bsattn_bf16_to_f16(v.data_ptr(), v16.data_ptr(), v.numel(),
+                                        torch.cuda.current_stream(dev).cuda_stream)
+        if rc != 0:
+            raise BsattnError(rc, "bsattn_bf16_to_f16")
+        v = v16
     nqb = T // BLOCK_SIZE
     rp, rp_stride = _bh_view(row_ptr.to(dev), B, H, "row_ptr")
     ci, ci_stride = _bh_view(col_idx.to(dev), B, H, "col_idx")
@@ -178,8 +196,7 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
             lse.data_ptr() if lse is not None else None,
             rp.data_ptr(), ci.data_ptr(), sl.data_ptr() if sl is not None else None,
             B, H, T, D, rp_stride, ci_stride, max_nnz,
-            float(scale) if scale is not None else 0.0,
-            _lib.OUT_BF16 if out_dtype == torch.bfloat16 else _lib.OUT_F16,
+            float(scale) if scale is not None else 0.0, flags,
             ws.data_ptr(), ws.numel() * 4, stream)
     if rc != 0:
         raise BsattnError(rc, "bsattn_fwd")

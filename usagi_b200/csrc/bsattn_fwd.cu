@@ -75,6 +75,7 @@ constexpr int kPolyEvery = 4;              // every 4th pair of exponentials run
 constexpr unsigned long long kDrainNs = 100000000ull;
 constexpr int kWsInts = 64;                // workspace: int32[64]
 constexpr uint32_t kIdescQK = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/false);
+constexpr uint32_t kIdescQKBf16 = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/false, true);
 constexpr uint32_t kIdescPV = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/true);
 // setmaxnreg budgets.  An increase draws only on the registers the block was launched with
 // (512 threads x 128), so per SMSP lane-slot (one warp of each warpgroup) the four budgets must
@@ -124,6 +125,7 @@ struct FwdParams {
   int group_heads;  // heads per item group (their K/V stay in L2 while the group is processed)
   float scale_log2;
   int out_bf16;
+  uint32_t idesc_qk;  // Q K^T instruction descriptor: fp16 or bf16 operands, fp32 accumulator
   unsigned long long timeout_ns;
   int test_unsignalled_wait;  // test hook: the QK^T issuer first waits on a barrier nobody signals
 };
@@ -404,7 +406,7 @@ __device__ void mma_s_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem)
 #pragma unroll
     for (int kk = 0; kk < kHd / 16; ++kk) {
       const uint32_t off = ((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4;
-      ptx::mma_ss(d, qd + off, kd + off, kIdescQK, kk > 0 ? 1u : 0u);
+      ptx::mma_ss(d, qd + off, kd + off, p.idesc_qk, kk > 0 ? 1u : 0u);
     }
     ptx::tc_commit(kv_empty0 + stage * 8);
     ptx::tc_commit(ptx::smem_u32(&sh.s_full[sb]));
@@ -784,14 +786,15 @@ static EncodeTiledFn get_encode_fn() {
 // strides {256 B per row, 128 B per half}: one box {64, 128, 2} moves a whole 128x128 tile and
 // lands it as two 16 KB blocks (columns 0..63 of all rows, then 64..127), each in the 128-byte
 // swizzled K-major layout the MMA descriptors address.
-static int make_tile_map(CUtensorMap* map, const void* base, uint64_t rows) {
+static int make_tile_map(CUtensorMap* map, const void* base, uint64_t rows, bool bf16) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return BSATTN_E_TMA;
   cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), 2};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHd * 2), 128};
   cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kBlk), 2};
   cuuint32_t estr[3] = {1, 1, 1};
-  CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base), dims, strides,
+  CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
+                   const_cast<void*>(base), dims, strides,
                    box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS ? BSATTN_OK : BSATTN_E_TMA;
@@ -843,6 +846,28 @@ static int device_setup(int* sms_out) {
 
 using namespace bsattn;
 
+// ------------------------------------------------------------------------------------------
+// bf16 -> fp16 conversion of V.  With bf16 inputs the reference computes Q K^T on bf16 operands
+// and P V as fp16(P) . fp16(V) (v4 :103, :123); the tensor cores take both operands of one MMA in
+// the same type, so V is converted once, up front, to the fp16 the reference converts it to.
+// Eight elements per thread and step (16-byte loads and stores), grid-stride.
+// ------------------------------------------------------------------------------------------
+__global__ void __launch_bounds__(256) bf16_to_f16_kernel(const uint4* __restrict__ src,
+                                                          uint4* __restrict__ dst, long long n8) {
+  for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n8; i += 256ll * gridDim.x) {
+    const uint4 a = src[i];
+    const uint32_t in[4] = {a.x, a.y, a.z, a.w};
+    uint32_t out[4];
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&in[w]));
+      __half2 h = __floats2half2_rn(f.x, f.y);
+      out[w] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    dst[i] = make_uint4(out[0], out[1], out[2], out[3]);
+  }
+}
+
 extern "C" {
 
 size_t bsattn_workspace_bytes(void) { return kWsInts * sizeof(int); }
@@ -850,6 +875,22 @@ size_t bsattn_workspace_bytes(void) { return kWsInts * sizeof(int); }
 int bsattn_version(void) { return 100; }
 
 void bsattn_set_timeout_ns(uint64_t ns) { g_timeout_ns = ns > 0 ? ns : 1; }
+
+int bsattn_bf16_to_f16(const void* src, void* dst, int64_t n, void* stream) {
+  if (!src || !dst) return BSATTN_E_NULL;
+  if (n < 0 || (n % 8) != 0) return BSATTN_E_SHAPE;
+  if ((reinterpret_cast<uintptr_t>(src) & 15u) != 0 || (reinterpret_cast<uintptr_t>(dst) & 15u) != 0)
+    return BSATTN_E_ALIGN;
+  if (n == 0) return BSATTN_OK;
+  int sms = 0;
+  const int rc = device_setup(&sms);
+  if (rc != BSATTN_OK) return rc;
+  const long long n8 = n / 8;
+  const int grid = static_cast<int>(std::min<long long>((n8 + 255) / 256, 8ll * sms));
+  bf16_to_f16_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint4*>(src), static_cast<uint4*>(dst), n8);
+  return cudaGetLastError() == cudaSuccess ? BSATTN_OK : BSATTN_E_CUDA;
+}
 
 void bsattn_test_unsignalled_wait(int enable) { g_test_unsignalled_wait = enable ? 1 : 0; }
 
@@ -875,7 +916,7 @@ const char* bsattn_strerror(int code) {
 int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
                const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens, int B,
                int H, int T, int D, int64_t rp_stride_bh, int64_t ci_stride_bh, int max_nnz,
-               float scale, int out_dtype, void* workspace, size_t workspace_bytes,
+               float scale, int dtype_flags, void* workspace, size_t workspace_bytes,
                void* stream) {
   if (!q || !k || !v || !o || !row_ptr || !col_idx) return BSATTN_E_NULL;
   if (B < 1 || H < 1 || T < kBlk || (T % kBlk) != 0 || D != kHd) return BSATTN_E_SHAPE;
@@ -883,7 +924,8 @@ int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   const long long rows = static_cast<long long>(B) * H * T;
   const long long items = static_cast<long long>(B) * H * (T / kBlk);
   if (rows >= (1ll << 31) || items >= (1ll << 30)) return BSATTN_E_SHAPE;
-  if (out_dtype != BSATTN_OUT_F16 && out_dtype != BSATTN_OUT_BF16) return BSATTN_E_DTYPE;
+  if ((dtype_flags & ~(BSATTN_OUT_BF16 | BSATTN_IN_BF16)) != 0) return BSATTN_E_DTYPE;
+  const bool qk_bf16 = (dtype_flags & BSATTN_IN_BF16) != 0;
   auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
   if (misaligned(q) || misaligned(k) || misaligned(v) || misaligned(o)) return BSATTN_E_ALIGN;
   if (!workspace || workspace_bytes < bsattn_workspace_bytes()) return BSATTN_E_WORKSPACE;
@@ -893,9 +935,9 @@ int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   if (rc != BSATTN_OK) return rc;
 
   CUtensorMap tq, tk, tv;
-  if ((rc = make_tile_map(&tq, q, rows)) != BSATTN_OK) return rc;
-  if ((rc = make_tile_map(&tk, k, rows)) != BSATTN_OK) return rc;
-  if ((rc = make_tile_map(&tv, v, rows)) != BSATTN_OK) return rc;
+  if ((rc = make_tile_map(&tq, q, rows, qk_bf16)) != BSATTN_OK) return rc;
+  if ((rc = make_tile_map(&tk, k, rows, qk_bf16)) != BSATTN_OK) return rc;
+  if ((rc = make_tile_map(&tv, v, rows, false)) != BSATTN_OK) return rc;
 
   FwdParams p;
   memset(&p, 0, sizeof(p));
@@ -919,7 +961,8 @@ int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
       std::max<long long>(1, std::min<long long>(B * H, (32ll << 20) / head_kv_bytes)));
   const double sc = scale > 0.0f ? static_cast<double>(scale) : 1.0 / sqrt(static_cast<double>(D));
   p.scale_log2 = static_cast<float>(sc * 1.4426950408889634);
-  p.out_bf16 = out_dtype == BSATTN_OUT_BF16 ? 1 : 0;
+  p.out_bf16 = (dtype_flags & BSATTN_OUT_BF16) != 0 ? 1 : 0;
+  p.idesc_qk = qk_bf16 ? kIdescQKBf16 : kIdescQK;
   p.timeout_ns = g_timeout_ns;
   p.test_unsignalled_wait = g_test_unsignalled_wait;
 
@@ -988,7 +1031,7 @@ extern "C" {
 int bsattn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
                        const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens,
                        int B, int H, int T, int D, int64_t rp_stride_bh, int64_t ci_stride_bh,
-                       int max_nnz, float scale, int out_dtype, int* status, void* stream) {
+                       int max_nnz, float scale, int dtype_flags, int* status, void* stream) {
   // The workspace the kernel needs must fit the fixed scratch array.
   if (bsattn_workspace_bytes() > kNoAllocScratchBytes) return BSATTN_E_WORKSPACE;
   void* scratch = nullptr;
@@ -998,7 +1041,7 @@ int bsattn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, flo
   // The scratch keeps the previous call's contents; the error word must start at zero.
   if (cudaMemsetAsync(scratch, 0, sizeof(int), s) != cudaSuccess) return BSATTN_E_CUDA;
   rc = bsattn_fwd(q, k, v, o, lse, row_ptr, col_idx, seq_lens, B, H, T, D, rp_stride_bh,
-                  ci_stride_bh, max_nnz, scale, out_dtype, scratch, kNoAllocScratchBytes, stream);
+                  ci_stride_bh, max_nnz, scale, dtype_flags, scratch, kNoAllocScratchBytes, stream);
   if (rc != BSATTN_OK) return rc;
   if (status != nullptr &&
       cudaMemcpyAsync(status, scratch, sizeof(int), cudaMemcpyDefault, s) != cudaSuccess)
