@@ -127,6 +127,23 @@ BSATTN_API void bsattn_test_unsignalled_wait(int enable);
  * done once per call instead of per tile.  n % 8 == 0; src and dst 16-byte aligned. */
 BSATTN_API int bsattn_bf16_to_f16(const void* src, void* dst, int64_t n, void* stream);
 
+/* CSR patterns built on the device.  No counterpart in the reference, which received row_ptr /
+ * col_idx from its harness (kernels/v4_leaderboard_0740ms.py:242); these build the families the
+ * harness used.  Every row is ascending and ends with its diagonal (v4 :78-86, :107).
+ *   BSATTN_CSR_WINDOW         row i = max(0, i-window+1) .. i                      (prefix == 0)
+ *   BSATTN_CSR_PREFIX_WINDOW  row i = {0 .. min(prefix-1, i)} U {max(0, i-window+1) .. i}
+ *   BSATTN_CSR_RETRIEVAL      row i = {i-1, i} U min(n_random, i-1) distinct blocks of 0 .. i-2,
+ *                             drawn from a counter-based generator keyed by (seed, head, row)
+ * bsattn_csr_nnz gives the column count of one head (row_ptr[nqb]); col_idx rows are ci_stride
+ * apart (ci_stride >= nnz), row_ptr is [n_heads, nqb + 1] contiguous.  The window families do not
+ * depend on the head or the seed: build one head and share it (stride 0). */
+enum { BSATTN_CSR_WINDOW = 0, BSATTN_CSR_PREFIX_WINDOW = 1, BSATTN_CSR_RETRIEVAL = 2 };
+BSATTN_API int bsattn_csr_nnz(int kind, int nqb, int prefix, int window, int n_random,
+                              int64_t* nnz);
+BSATTN_API int bsattn_build_csr(int kind, int nqb, int prefix, int window, int n_random,
+                                uint64_t seed, int n_heads, int32_t* row_ptr, int32_t* col_idx,
+                                int64_t ci_stride, void* stream);
+
 /* Human-readable text for a BSATTN_E* code. */
 BSATTN_API const char* bsattn_strerror(int code);
 

@@ -61,3 +61,46 @@ def test_prefix_window_rows():
     r = P.prefix_window_rows(10, 4, 4)
     assert r[0] == [0] and r[3] == [0, 1, 2, 3] and r[4] == [0, 1, 2, 3, 4]
     assert r[9] == [0, 1, 2, 3, 6, 7, 8, 9]
+
+
+# --- the library's device CSR builder: host-side pieces (closed-form offsets, validation) ---
+def _nnz(kind, nqb, prefix=0, window=0, n_random=0):
+    import ctypes
+    from usagi_b200 import _lib
+    v = ctypes.c_int64(-1)
+    rc = _lib.load().bsattn_csr_nnz(kind, nqb, prefix, window, n_random, ctypes.byref(v))
+    return rc, v.value
+
+
+def test_device_builder_row_offsets_match_host_builder():
+    """row_ptr[i] of the device builder is the column count of the first i rows, i.e. nnz of a
+    pattern with i rows; it must equal the host builder's row_ptr for every i."""
+    from usagi_b200 import _lib
+    n = 70
+    cases = [(_lib.CSR_WINDOW, dict(window=8), P.window_pattern(1, 1, n * 128, 8)),
+             (_lib.CSR_WINDOW, dict(window=1), P.window_pattern(1, 1, n * 128, 1)),
+             (_lib.CSR_PREFIX_WINDOW, dict(prefix=4, window=4), P.prefix_window_pattern(1, 1, n * 128, 4, 4)),
+             (_lib.CSR_PREFIX_WINDOW, dict(prefix=8, window=8), P.prefix_window_pattern(1, 1, n * 128, 8, 8)),
+             (_lib.CSR_RETRIEVAL, dict(n_random=8), P.retrieval_pattern(1, 1, n * 128, 8)),
+             (_lib.CSR_RETRIEVAL, dict(n_random=16), P.retrieval_pattern(1, 1, n * 128, 16))]
+    for kind, kw, pat in cases:
+        rp = pat.row_ptr.reshape(-1)
+        for i in range(1, n + 1):
+            rc, v = _nnz(kind, i, **kw)
+            assert rc == 0 and v == int(rp[i]), (kind, kw, i, v, int(rp[i]))
+
+
+def test_device_builder_validation():
+    from usagi_b200 import _lib
+    lib = _lib.load()
+    assert _nnz(7, 8, window=4)[0] == _lib.E_SHAPE
+    assert _nnz(_lib.CSR_WINDOW, 0, window=4)[0] == _lib.E_SHAPE
+    assert _nnz(_lib.CSR_WINDOW, 8, window=0)[0] == _lib.E_SHAPE
+    assert _nnz(_lib.CSR_WINDOW, 8, prefix=2, window=4)[0] == _lib.E_SHAPE
+    assert _nnz(_lib.CSR_RETRIEVAL, 8, n_random=65)[0] == _lib.E_SHAPE
+    assert _nnz(_lib.CSR_RETRIEVAL, 8, n_random=-1)[0] == _lib.E_SHAPE
+    assert lib.bsattn_csr_nnz(_lib.CSR_WINDOW, 8, 0, 4, 0, None) == _lib.E_NULL
+    # argument errors are returned before anything touches a device
+    assert lib.bsattn_build_csr(_lib.CSR_WINDOW, 8, 0, 4, 0, 1, 1, None, 16, 64, None) == _lib.E_NULL
+    assert lib.bsattn_build_csr(_lib.CSR_WINDOW, 8, 0, 4, 0, 1, 1, 16, 16, 3, None) == _lib.E_SHAPE
+    assert lib.bsattn_build_csr(_lib.CSR_WINDOW, 8, 0, 4, 0, 1, 0, 16, 16, 64, None) == _lib.E_SHAPE

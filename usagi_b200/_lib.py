@@ -31,6 +31,10 @@ SIGNATURES = {
     ]),
     "bsattn_check_error": (_c_int, [_c_void_p, _c_void_p, ctypes.POINTER(_c_int)]),
     "bsattn_bf16_to_f16": (_c_int, [_c_void_p, _c_void_p, ctypes.c_int64, _c_void_p]),
+    "bsattn_csr_nnz": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int,
+                                ctypes.POINTER(ctypes.c_int64)]),
+    "bsattn_build_csr": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.c_uint64,
+                                  _c_int, _c_void_p, _c_void_p, ctypes.c_int64, _c_void_p]),
     "bsattn_fwd_noalloc": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p,          # q, k, v
         _c_void_p, _c_void_p,                     # o, lse
@@ -47,6 +51,7 @@ OK = 0
 E_SHAPE, E_ALIGN, E_NULL, E_WORKSPACE, E_CUDA, E_TMA, E_DEVICE, E_CSR, E_TIMEOUT, E_DTYPE = (
     -1, -2, -3, -4, -5, -6, -7, -8, -9, -10)
 OUT_F16, OUT_BF16, IN_BF16 = 0, 1, 2
+CSR_WINDOW, CSR_PREFIX_WINDOW, CSR_RETRIEVAL = 0, 1, 2
 
 _lock = threading.Lock()
 _lib = None

@@ -21,7 +21,7 @@ INCLUDE = PKG_DIR.parent / "include"
 LIB_NAME = "libbsattn.so"
 LIB_PATH = PKG_DIR / LIB_NAME
 
-SOURCES = ["bsattn_fwd.cu"]
+SOURCES = ["bsattn_fwd.cu", "csr_build.cu"]
 HEADERS = ["sm100_ptx.cuh"]
 
 NVCC_FLAGS = [

@@ -42,6 +42,9 @@ __all__ = [
     "family_pattern",
     "live_blocks",
     "FAMILIES",
+    "device_window_pattern",
+    "device_prefix_window_pattern",
+    "device_retrieval_pattern",
 ]
 
 
@@ -205,3 +208,55 @@ def family_pattern(name: str, B: int, H: int, T: int) -> CsrPattern:
 
 def live_blocks(pattern: CsrPattern) -> int:
     return pattern.live_blocks()
+
+
+# ---------------------------------------------------------------------------------------------
+# The same families built on the GPU by the library (bsattn_build_csr), for callers that keep the
+# whole step on the device.  Window families are bit-identical to the host builders above and are
+# built once and shared by every head (stride 0); retrieval rows use the library's counter-based
+# generator keyed by (seed, head, row): the same distribution as retrieval_rows, other draws.
+# ---------------------------------------------------------------------------------------------
+def _device_csr(kind: int, n_heads: int, nqb: int, prefix: int, window: int, n_random: int,
+                seed: int, device) -> tuple:
+    import ctypes
+    from . import _lib
+    lib = _lib.load()
+    nnz = ctypes.c_int64(0)
+    rc = lib.bsattn_csr_nnz(kind, nqb, prefix, window, n_random, ctypes.byref(nnz))
+    if rc != 0:
+        raise ValueError(f"bsattn_csr_nnz: {_lib.strerror(rc)}")
+    dev = torch.device(device)
+    rp = torch.empty((n_heads, nqb + 1), dtype=torch.int32, device=dev)
+    ci = torch.empty((n_heads, max(int(nnz.value), 1)), dtype=torch.int32, device=dev)
+    with torch.cuda.device(dev):
+        rc = lib.bsattn_build_csr(kind, nqb, prefix, window, n_random,
+                                  seed & 0xFFFFFFFFFFFFFFFF, n_heads, rp.data_ptr(),
+                                  ci.data_ptr(), ci.shape[1],
+                                  torch.cuda.current_stream(dev).cuda_stream)
+    if rc != 0:
+        raise RuntimeError(f"bsattn_build_csr: {_lib.strerror(rc)}")
+    return rp, ci
+
+
+def device_window_pattern(B: int, H: int, T: int, window: int = 8,
+                          device="cuda") -> CsrPattern:
+    nqb = T // BLOCK
+    rp, ci = _device_csr(0, 1, nqb, 0, window, 0, 0, device)
+    return CsrPattern(rp.reshape(1, 1, -1).expand(B, H, nqb + 1),
+                      ci.reshape(1, 1, -1).expand(B, H, ci.shape[1]), f"window{window}")
+
+
+def device_prefix_window_pattern(B: int, H: int, T: int, prefix: int = 4, window: int = 4,
+                                 device="cuda") -> CsrPattern:
+    nqb = T // BLOCK
+    rp, ci = _device_csr(1, 1, nqb, prefix, window, 0, 0, device)
+    return CsrPattern(rp.reshape(1, 1, -1).expand(B, H, nqb + 1),
+                      ci.reshape(1, 1, -1).expand(B, H, ci.shape[1]),
+                      f"prefix{prefix}+window{window}")
+
+
+def device_retrieval_pattern(B: int, H: int, T: int, n_random: int = 8, seed: int = 1,
+                             device="cuda") -> CsrPattern:
+    nqb = T // BLOCK
+    rp, ci = _device_csr(2, B * H, nqb, 0, 0, n_random, seed, device)
+    return CsrPattern(rp.reshape(B, H, nqb + 1), ci.reshape(B, H, -1), f"retrieval{n_random}")
