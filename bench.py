@@ -241,9 +241,11 @@ def measure_e2e(ub, inputs, outs, lses, flops_step, device, world, args):
     import torch.distributed as dist
     host_in, host_out = {}, {}
     for f in FAMILIES:
-        q, k, v, rp, ci = inputs[f]
+        q, k, v, rp, ci, plan = inputs[f]
         host_in[f] = [t.cpu().pin_memory() for t in (q, k, v)] + [rp.cpu().pin_memory(),
                                                                   ci.cpu().pin_memory()]
+        if plan is not None:
+            host_in[f].append(plan.tensor.cpu().pin_memory())
         host_out[f] = (torch.empty(outs[f].shape, dtype=torch.float16).pin_memory(),
                        torch.empty(lses[f].shape, dtype=torch.float32).pin_memory())
     h2d = sum(t.numel() * t.element_size() for f in FAMILIES for t in host_in[f])
@@ -251,11 +253,16 @@ def measure_e2e(ub, inputs, outs, lses, flops_step, device, world, args):
 
     def e2e_step():
         for f in FAMILIES:
-            hq, hk, hv, hrp, hci = host_in[f]
+            hq, hk, hv, hrp, hci = host_in[f][:5]
             dq, dk, dv = (hq.to(device, non_blocking=True), hk.to(device, non_blocking=True),
                           hv.to(device, non_blocking=True))
             drp, dci = hrp.to(device, non_blocking=True), hci.to(device, non_blocking=True)
-            o, lse = ub.block_sparse_attn_fwd(dq, dk, dv, drp, dci, None)
+            plan = None
+            if len(host_in[f]) > 5:
+                p0 = inputs[f][5]
+                plan = ub.Plan(host_in[f][5].to(device, non_blocking=True), p0.grid, p0.B, p0.H,
+                               p0.T)
+            o, lse = ub.block_sparse_attn_fwd(dq, dk, dv, drp, dci, None, plan=plan)
             host_out[f][0].copy_(o, non_blocking=True)
             host_out[f][1].copy_(lse, non_blocking=True)
 
@@ -294,6 +301,8 @@ def main():
                     help="seconds of CPU work per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true")
+    ap.add_argument("--no-plan", action="store_true",
+                    help="round-robin item order instead of the balanced work list")
     ap.add_argument("--family", choices=FAMILIES, default=None,
                     help="run one family only (profiling); the JSON line then covers that family")
     ap.add_argument("--quick", action="store_true",
@@ -344,7 +353,11 @@ def main():
     inputs = {}
     for fam in FAMILIES:
         q, k, v, pat = make_inputs(device, rank, fam)
-        inputs[fam] = (q, k, v, pat.row_ptr.to(device), pat.col_idx.to(device))
+        # The balanced work list is built once per pattern on the host (bsattn_plan), like the
+        # pattern itself; --no-plan keeps the round-robin item order.
+        plan = None if args.no_plan else ub.make_plan(pat.row_ptr, pat.col_idx, B_PER_RANK, H, T,
+                                                      device=device)
+        inputs[fam] = (q, k, v, pat.row_ptr.to(device), pat.col_idx.to(device), plan)
     flops = {f: _pattern_flops(f) for f in FAMILIES}
     flops_step = sum(flops.values())
     outs = {f: torch.empty((B_PER_RANK, H, T, D), device=device, dtype=torch.float16)
@@ -354,8 +367,8 @@ def main():
     flush = torch.empty(512 * 1024 * 1024 // 4, device=device, dtype=torch.float32)
 
     def call(f):
-        q, k, v, rp, ci = inputs[f]
-        ub.block_sparse_attn_fwd(q, k, v, rp, ci, None, out=outs[f], lse_out=lses[f])
+        q, k, v, rp, ci, plan = inputs[f]
+        ub.block_sparse_attn_fwd(q, k, v, rp, ci, None, out=outs[f], lse_out=lses[f], plan=plan)
 
     for _ in range(args.warmup):
         for f in FAMILIES:
@@ -426,6 +439,7 @@ def main():
             "global_batch": B_PER_RANK * world, "heads": H, "seq_len": T, "head_dim": D,
             "parallelism": f"head-sharded x{world} (batch entries split across ranks, no collective)",
             "l2": "flushed (512 MB write) before every timed call",
+            "schedule": "round robin" if args.no_plan else "balanced work list (bsattn_plan)",
         },
         "ms_per_call": fam_ms,
         "ms_per_call_geomean": geo_ms,

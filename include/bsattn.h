@@ -55,7 +55,8 @@ enum {
   BSATTN_E_DEVICE = -7,     /* current device is not an sm_100 part                         */
   BSATTN_E_CSR = -8,        /* (device-reported) CSR row or column index out of range       */
   BSATTN_E_TIMEOUT = -9,    /* (device-reported) a pipeline wait exceeded its time limit    */
-  BSATTN_E_DTYPE = -10      /* unsupported dtype code                                       */
+  BSATTN_E_DTYPE = -10,     /* unsupported dtype code                                       */
+  BSATTN_E_PLAN = -11       /* work list does not match the call (or has an id out of range) */
 };
 
 /* dtype_flags of bsattn_fwd: element types of the inputs and of `o`, OR-ed together.
@@ -79,6 +80,27 @@ BSATTN_API int bsattn_fwd(const void* q, const void* k, const void* v, void* o, 
                int64_t rp_stride_bh, int64_t ci_stride_bh, int max_nnz,
                float scale, int dtype_flags,
                void* workspace, size_t workspace_bytes, void* stream);
+
+/* bsattn_fwd with an optional work list (plan, device memory, from bsattn_plan for the same B, H,
+ * T, row_ptr and seq_lens; plan_grid = the grid it was built for).  plan == NULL is bsattn_fwd.
+ * Replaces the reference's fixed (qb, b*h) program grid (kernels/v4_leaderboard_0740ms.py:166-177)
+ * with a persistent grid whose CTAs take balanced item lists.  A list that does not match the
+ * call is reported as BSATTN_E_PLAN through bsattn_check_error and the kernel does no work. */
+BSATTN_API int bsattn_fwd_plan(const void* q, const void* k, const void* v, void* o, float* lse,
+                               const int32_t* row_ptr, const int32_t* col_idx,
+                               const int32_t* seq_lens, int B, int H, int T, int D,
+                               int64_t rp_stride_bh, int64_t ci_stride_bh, int max_nnz,
+                               float scale, int dtype_flags, const int32_t* plan, int plan_grid,
+                               void* workspace, size_t workspace_bytes, void* stream);
+
+/* Work list for bsattn_fwd_plan, built on the host (row_ptr and seq_lens are HOST arrays, laid
+ * out as for bsattn_fwd).  Items are sorted by tile count, largest first, and dealt to `grid`
+ * CTAs in snake order, which keeps every CTA within one item of the mean.  Build it once per
+ * pattern, copy it to the device, reuse it.  bsattn_plan_bytes gives the size in bytes. */
+BSATTN_API int bsattn_plan_bytes(int B, int H, int T, int grid, size_t* bytes);
+BSATTN_API int bsattn_plan(const int32_t* row_ptr, int64_t rp_stride_bh, const int32_t* seq_lens,
+                           int B, int H, int T, int max_nnz, int grid, int32_t* plan,
+                           size_t plan_bytes);
 
 /* Allocation-free variant of bsattn_fwd.  No counterpart in the reference: its Python entry
  * point allocated outputs and metadata with torch on every call.

@@ -42,7 +42,7 @@ def test_version_workspace_strerror():
     lib = _lib.load()
     assert lib.bsattn_version() == 100
     assert lib.bsattn_workspace_bytes() >= 4
-    for code in range(0, -11, -1):
+    for code in range(0, -12, -1):
         assert _lib.strerror(code) != "unknown error"
     assert _lib.strerror(-99) == "unknown error"
 

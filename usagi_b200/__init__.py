@@ -7,7 +7,9 @@ Drop-in for the ``block_sparse_attn_fwd`` submission API of sissississi-013/usag
 from .api import (  # noqa: F401
     VARIANT_MANIFEST,
     BsattnError,
+    Plan,
     block_sparse_attn_fwd,
+    make_plan,
     check_errors,
     set_timeout_ns,
     setup,

@@ -30,6 +30,19 @@ SIGNATURES = {
         _c_void_p, _c_size_t, _c_void_p,          # workspace, bytes, stream
     ]),
     "bsattn_check_error": (_c_int, [_c_void_p, _c_void_p, ctypes.POINTER(_c_int)]),
+    "bsattn_fwd_plan": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p,          # q, k, v
+        _c_void_p, _c_void_p,                     # o, lse
+        _c_void_p, _c_void_p, _c_void_p,          # row_ptr, col_idx, seq_lens
+        _c_int, _c_int, _c_int, _c_int,           # B, H, T, D
+        ctypes.c_int64, ctypes.c_int64, _c_int,   # rp_stride_bh, ci_stride_bh, max_nnz
+        ctypes.c_float, _c_int,                   # scale, dtype_flags
+        _c_void_p, _c_int,                        # plan (device), plan_grid
+        _c_void_p, _c_size_t, _c_void_p,          # workspace, bytes, stream
+    ]),
+    "bsattn_plan_bytes": (_c_int, [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_size_t)]),
+    "bsattn_plan": (_c_int, [_c_void_p, ctypes.c_int64, _c_void_p, _c_int, _c_int, _c_int, _c_int,
+                             _c_int, _c_void_p, _c_size_t]),
     "bsattn_bf16_to_f16": (_c_int, [_c_void_p, _c_void_p, ctypes.c_int64, _c_void_p]),
     "bsattn_csr_nnz": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int,
                                 ctypes.POINTER(ctypes.c_int64)]),
@@ -50,6 +63,7 @@ SIGNATURES = {
 OK = 0
 E_SHAPE, E_ALIGN, E_NULL, E_WORKSPACE, E_CUDA, E_TMA, E_DEVICE, E_CSR, E_TIMEOUT, E_DTYPE = (
     -1, -2, -3, -4, -5, -6, -7, -8, -9, -10)
+E_PLAN = -11
 OUT_F16, OUT_BF16, IN_BF16 = 0, 1, 2
 CSR_WINDOW, CSR_PREFIX_WINDOW, CSR_RETRIEVAL = 0, 1, 2
 

@@ -37,6 +37,8 @@ __all__ = [
     "block_sparse_attn_fwd",
     "check_errors",
     "set_timeout_ns",
+    "Plan",
+    "make_plan",
 ]
 
 BLOCK_SIZE = 128
@@ -119,6 +121,47 @@ def _bh_view(t: torch.Tensor, B: int, H: int, name: str) -> Tuple[torch.Tensor, 
     raise ValueError(f"{name}: expected 1-3 dims, got {t.dim()}")
 
 
+class Plan:
+    """Balanced work list for one problem shape and pattern (``bsattn_plan``), on the device.
+
+    Items (query blocks of a head) are sorted by tile count, largest first, and dealt to the
+    persistent CTAs in snake order, so every CTA ends within one item of the mean; without a plan
+    CTA b takes items b, b + grid, ...  Valid for the B, H, T, row_ptr, max_nnz and seq_lens it
+    was built from.
+    """
+
+    def __init__(self, tensor: torch.Tensor, grid: int, B: int, H: int, T: int):
+        self.tensor, self.grid, self.B, self.H, self.T = tensor, grid, B, H, T
+
+
+def make_plan(row_ptr: torch.Tensor, col_idx: torch.Tensor, B: int, H: int, T: int,
+              seq_lens: Optional[torch.Tensor] = None, device="cuda",
+              grid: Optional[int] = None) -> Plan:
+    """Build a :class:`Plan` on the host from the pattern (copied to the host once) and move it
+    to ``device``.  ``grid`` defaults to the persistent grid of the call: one CTA per SM."""
+    import ctypes
+    lib = _lib.load()
+    nqb = T // BLOCK_SIZE
+    rp, rp_stride = _bh_view(row_ptr.detach().cpu(), B, H, "row_ptr")
+    max_nnz = int(col_idx.shape[-1])
+    sl = None
+    if seq_lens is not None:
+        sl = seq_lens.detach().cpu().to(torch.int32).contiguous()
+    dev = torch.device(device)
+    if grid is None:
+        grid = min(torch.cuda.get_device_properties(dev).multi_processor_count, B * H * nqb)
+    nbytes = ctypes.c_size_t(0)
+    rc = lib.bsattn_plan_bytes(B, H, T, grid, ctypes.byref(nbytes))
+    if rc != 0:
+        raise BsattnError(rc, "bsattn_plan_bytes")
+    host = torch.empty(nbytes.value // 4, dtype=torch.int32)
+    rc = lib.bsattn_plan(rp.data_ptr(), rp_stride, sl.data_ptr() if sl is not None else None,
+                         B, H, T, max_nnz, grid, host.data_ptr(), nbytes.value)
+    if rc != 0:
+        raise BsattnError(rc, "bsattn_plan")
+    return Plan(host.to(dev), grid, B, H, T)
+
+
 def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                           row_ptr: torch.Tensor, col_idx: torch.Tensor,
                           seq_lens: Optional[torch.Tensor] = None, *,
@@ -126,14 +169,16 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                           out_dtype: Optional[torch.dtype] = None,
                           out: Optional[torch.Tensor] = None,
                           lse_out: Optional[torch.Tensor] = None,
-                          return_lse: bool = True):
+                          return_lse: bool = True,
+                          plan: Optional[Plan] = None):
     """Block-sparse causal attention forward on a B200.
 
     q, k: fp16 or bf16 [B, H, T, 128] CUDA tensors of one dtype, T % 128 == 0; v: the same shape,
     fp16 or the dtype of q.  row_ptr: int [B, H, T/128 + 1]; col_idx: int [B, H, max_nnz] (or
     [B*H, .], or one shared [.] row); seq_lens: int [B] or None.  Returns ``(o, lse)`` like the
     reference (v4 :179): o [B, H, T, 128] in ``out_dtype`` (default: q's dtype), lse fp32
-    [B, H, T] (None if ``return_lse=False``).
+    [B, H, T] (None if ``return_lse=False``).  ``plan`` (from :func:`make_plan` for this pattern)
+    balances the work across the persistent CTAs; results are identical with or without it.
     """
     lib = _lib.load()
     if q.dim() != 4:
@@ -191,12 +236,17 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
         ws = _workspace(dev, stream)
-        rc = lib.bsattn_fwd(
+        if plan is not None:
+            if (plan.B, plan.H, plan.T) != (B, H, T) or plan.tensor.device != dev:
+                raise ValueError("plan was built for another shape or device")
+        rc = lib.bsattn_fwd_plan(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
             lse.data_ptr() if lse is not None else None,
             rp.data_ptr(), ci.data_ptr(), sl.data_ptr() if sl is not None else None,
             B, H, T, D, rp_stride, ci_stride, max_nnz,
             float(scale) if scale is not None else 0.0, flags,
+            plan.tensor.data_ptr() if plan is not None else None,
+            plan.grid if plan is not None else 0,
             ws.data_ptr(), ws.numel() * 4, stream)
     if rc != 0:
         raise BsattnError(rc, "bsattn_fwd")

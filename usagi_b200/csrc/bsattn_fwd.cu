@@ -49,6 +49,7 @@
 
 #include <algorithm>
 #include <mutex>
+#include <vector>
 
 #include "../../include/bsattn.h"
 #include "sm100_ptx.cuh"
@@ -128,6 +129,7 @@ struct FwdParams {
   uint32_t idesc_qk;  // Q K^T instruction descriptor: fp16 or bf16 operands, fp32 accumulator
   unsigned long long timeout_ns;
   int test_unsignalled_wait;  // test hook: the QK^T issuer first waits on a barrier nobody signals
+  const int32_t* plan;        // optional work list built by bsattn_plan (null: round robin)
 };
 
 // One work item = one (head, query block).
@@ -167,8 +169,60 @@ __device__ __forceinline__ Item load_item(const FwdParams& p, int g, bool* csr_b
   return it;
 }
 
+// The items of this CTA, in processing order.  Without a work list CTA b takes items b, b + grid,
+// b + 2 grid, ...  A work list (bsattn_plan) is {magic, grid, total_items, 0}, then grid + 1
+// offsets, then item ids: CTA b takes list[off[b] .. off[b+1]).  Every role walks the same
+// sequence; a list that does not match this launch, or an id out of range, ends the CTA's work
+// and is reported as BSATTN_E_PLAN (every role reads the same entries, so all stop together).
+constexpr int32_t kPlanMagic = 0x4e4c5042;
+constexpr int kPlanHeader = 4;
+
+struct ItemCursor {
+  int k, end;
+};
+
+__device__ __forceinline__ void report_plan_error(const FwdParams& p) {
+  atomicCAS(p.ws, 0, BSATTN_E_PLAN);
+}
+
+__device__ __forceinline__ void cursor_begin(ItemCursor& c, const FwdParams& p) {
+  if (p.plan == nullptr) {
+    c.k = static_cast<int>(blockIdx.x);
+    c.end = p.total_items;
+    return;
+  }
+  const int32_t* h = p.plan;
+  const bool hdr = __ldg(h) == kPlanMagic && __ldg(h + 1) == static_cast<int>(gridDim.x) &&
+                   __ldg(h + 2) == p.total_items;
+  c.k = hdr ? __ldg(h + kPlanHeader + blockIdx.x) : 0;
+  c.end = hdr ? __ldg(h + kPlanHeader + blockIdx.x + 1) : 0;
+  if (!hdr || c.k < 0 || c.end < c.k || c.end > p.total_items) {
+    c.k = c.end = 0;
+    report_plan_error(p);
+  }
+}
+
+// Next item id of this CTA, or -1 when it has none left.
+__device__ __forceinline__ int cursor_next(ItemCursor& c, const FwdParams& p) {
+  if (c.k >= c.end) return -1;
+  if (p.plan == nullptr) {
+    const int g = c.k;
+    c.k += static_cast<int>(gridDim.x);
+    return g;
+  }
+  const int g = __ldg(p.plan + kPlanHeader + gridDim.x + 1 + c.k);
+  ++c.k;
+  if (g < 0 || g >= p.total_items) {
+    c.k = c.end;
+    report_plan_error(p);
+    return -1;
+  }
+  return g;
+}
+
 // Walks this CTA's tiles across its active items: tile t = (item counter ii, step j).
 struct TileIter {
+  ItemCursor cur;
   int g;      // global item index
   int ii;     // active-item counter (buffer parity = ii & 1)
   int j;      // step within the item
@@ -180,15 +234,15 @@ struct TileIter {
 
 __device__ __forceinline__ bool seek_active(TileIter& x, const FwdParams& p, bool* csr_bad) {
   for (;;) {
-    x.g += gridDim.x;
-    if (x.g >= p.total_items) return false;
+    x.g = cursor_next(x.cur, p);
+    if (x.g < 0) return false;
     x.it = load_item(p, x.g, csr_bad);
     if (x.it.n_steps > 0) return true;
   }
 }
 
 __device__ __forceinline__ void tile_begin(TileIter& x, const FwdParams& p, bool* csr_bad) {
-  x.g = static_cast<int>(blockIdx.x) - static_cast<int>(gridDim.x);
+  cursor_begin(x.cur, p);
   x.ii = 0;
   x.j = 0;
   x.t = 0;
@@ -470,7 +524,9 @@ __device__ void softmax_role(SharedStorage& sh, const FwdParams& p, int half, ui
   int tile = 0;
   int ii = 0;
 
-  for (int g = blockIdx.x; g < p.total_items; g += gridDim.x) {
+  ItemCursor cur;
+  cursor_begin(cur, p);
+  for (int g = cursor_next(cur, p); g >= 0; g = cursor_next(cur, p)) {
     const Item it = load_item(p, g, nullptr);
     if (it.n_steps == 0) continue;  // the epilogue warpgroup writes inactive items
     const int ob = ii & 1;
@@ -632,7 +688,9 @@ __device__ void epilogue_role(SharedStorage& sh, const FwdParams& p, uint32_t tm
   const int wq = t >> 5;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(wq * 32) << 16);
   int ii = 0;
-  for (int g = blockIdx.x; g < p.total_items; g += gridDim.x) {
+  ItemCursor cur;
+  cursor_begin(cur, p);
+  for (int g = cursor_next(cur, p); g >= 0; g = cursor_next(cur, p)) {
     const Item it = load_item(p, g, nullptr);
     const int q_pos = it.qb * kBlk + t;
     const size_t row = static_cast<size_t>(it.bh) * p.T + q_pos;
@@ -813,6 +871,26 @@ static int g_test_unsignalled_wait = 0;
 
 static size_t smem_bytes() { return sizeof(SharedStorage) + 1024; }
 
+// Heads per item group: K and V of one head take 2 * T * 128 * 2 bytes; keep a group's worth near
+// 32 MB of L2.
+static int group_heads_for(int B, int H, int T) {
+  const long long head_kv_bytes = 512ll * T;
+  return static_cast<int>(
+      std::max<long long>(1, std::min<long long>(static_cast<long long>(B) * H,
+                                                 (32ll << 20) / head_kv_bytes)));
+}
+
+// Host copy of the kernel's item order (load_item): item g -> (bh, qb).
+static void item_coords(int g, int BH, int nqb, int group_heads, int* bh, int* qb) {
+  const int per_group = group_heads * nqb;
+  const int grp = g / per_group;
+  const int r = g - grp * per_group;
+  const int gh = std::min(group_heads, BH - grp * group_heads);
+  const int band = r / gh;
+  *bh = grp * group_heads + (r - band * gh);
+  *qb = nqb - 1 - band;
+}
+
 static int device_setup(int* sms_out) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return BSATTN_E_CUDA;
@@ -908,16 +986,17 @@ const char* bsattn_strerror(int code) {
     case BSATTN_E_DEVICE: return "device is not an sm_100 (B200-class) GPU";
     case BSATTN_E_CSR: return "CSR row_ptr/col_idx entry out of range";
     case BSATTN_E_TIMEOUT: return "kernel pipeline wait timed out";
-    case BSATTN_E_DTYPE: return "unsupported output dtype";
+    case BSATTN_E_DTYPE: return "unsupported dtype flags";
+    case BSATTN_E_PLAN: return "work list does not match this call";
     default: return "unknown error";
   }
 }
 
-int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
-               const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens, int B,
-               int H, int T, int D, int64_t rp_stride_bh, int64_t ci_stride_bh, int max_nnz,
-               float scale, int dtype_flags, void* workspace, size_t workspace_bytes,
-               void* stream) {
+int bsattn_fwd_plan(const void* q, const void* k, const void* v, void* o, float* lse,
+                    const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens,
+                    int B, int H, int T, int D, int64_t rp_stride_bh, int64_t ci_stride_bh,
+                    int max_nnz, float scale, int dtype_flags, const int32_t* plan, int plan_grid,
+                    void* workspace, size_t workspace_bytes, void* stream) {
   if (!q || !k || !v || !o || !row_ptr || !col_idx) return BSATTN_E_NULL;
   if (B < 1 || H < 1 || T < kBlk || (T % kBlk) != 0 || D != kHd) return BSATTN_E_SHAPE;
   if (max_nnz < 0 || rp_stride_bh < 0 || ci_stride_bh < 0) return BSATTN_E_SHAPE;
@@ -929,6 +1008,9 @@ int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   auto misaligned = [](const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 15u) != 0; };
   if (misaligned(q) || misaligned(k) || misaligned(v) || misaligned(o)) return BSATTN_E_ALIGN;
   if (!workspace || workspace_bytes < bsattn_workspace_bytes()) return BSATTN_E_WORKSPACE;
+  if (plan != nullptr && ((reinterpret_cast<uintptr_t>(plan) & 3u) != 0 || plan_grid < 1 ||
+                          plan_grid > items))
+    return BSATTN_E_PLAN;
 
   int sms = 0;
   int rc = device_setup(&sms);
@@ -955,21 +1037,97 @@ int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
   p.T = T;
   p.nqb = T / kBlk;
   p.total_items = static_cast<int>(items);
-  // K and V of one head take 2 * T * 128 * 2 bytes; keep a group's worth near 32 MB of L2.
-  const long long head_kv_bytes = 512ll * T;
-  p.group_heads = static_cast<int>(
-      std::max<long long>(1, std::min<long long>(B * H, (32ll << 20) / head_kv_bytes)));
+  p.group_heads = group_heads_for(B, H, T);
   const double sc = scale > 0.0f ? static_cast<double>(scale) : 1.0 / sqrt(static_cast<double>(D));
   p.scale_log2 = static_cast<float>(sc * 1.4426950408889634);
   p.out_bf16 = (dtype_flags & BSATTN_OUT_BF16) != 0 ? 1 : 0;
   p.idesc_qk = qk_bf16 ? kIdescQKBf16 : kIdescQK;
   p.timeout_ns = g_timeout_ns;
   p.test_unsignalled_wait = g_test_unsignalled_wait;
+  p.plan = plan;
 
-  const int grid = static_cast<int>(std::min<long long>(sms, items));
+  const int grid = plan != nullptr ? plan_grid : static_cast<int>(std::min<long long>(sms, items));
   bsattn_fwd_kernel<<<grid, kThreads, smem_bytes(), static_cast<cudaStream_t>(stream)>>>(tq, tk,
                                                                                         tv, p);
   return cudaGetLastError() == cudaSuccess ? BSATTN_OK : BSATTN_E_CUDA;
+}
+
+int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+               const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens, int B,
+               int H, int T, int D, int64_t rp_stride_bh, int64_t ci_stride_bh, int max_nnz,
+               float scale, int dtype_flags, void* workspace, size_t workspace_bytes,
+               void* stream) {
+  return bsattn_fwd_plan(q, k, v, o, lse, row_ptr, col_idx, seq_lens, B, H, T, D, rp_stride_bh,
+                         ci_stride_bh, max_nnz, scale, dtype_flags, nullptr, 0, workspace,
+                         workspace_bytes, stream);
+}
+
+int bsattn_plan_bytes(int B, int H, int T, int grid, size_t* bytes) {
+  if (!bytes) return BSATTN_E_NULL;
+  if (B < 1 || H < 1 || T < kBlk || (T % kBlk) != 0) return BSATTN_E_SHAPE;
+  const long long items = static_cast<long long>(B) * H * (T / kBlk);
+  if (items >= (1ll << 30) || grid < 1 || grid > items) return BSATTN_E_SHAPE;
+  *bytes = static_cast<size_t>(kPlanHeader + grid + 1 + items) * sizeof(int32_t);
+  return BSATTN_OK;
+}
+
+// Work list: items sorted by their tile count, largest first (ties keep the kernel's item order,
+// so the big items stay grouped by head for L2 reuse), dealt to the CTAs in a snake order
+// (0 .. grid-1, then grid-1 .. 0, ...).  Each CTA keeps its items in that sorted order.  The tile
+// count of an item is the kernel's: 0 past seq_len, else the listed off-diagonal blocks plus the
+// diagonal (rows whose range does not fit col_idx count as the diagonal alone, as in load_item).
+int bsattn_plan(const int32_t* row_ptr, int64_t rp_stride_bh, const int32_t* seq_lens, int B,
+                int H, int T, int max_nnz, int grid, int32_t* plan, size_t plan_bytes) {
+  if (!row_ptr || !plan) return BSATTN_E_NULL;
+  size_t need = 0;
+  int rc = bsattn_plan_bytes(B, H, T, grid, &need);
+  if (rc != BSATTN_OK) return rc;
+  if (plan_bytes < need) return BSATTN_E_WORKSPACE;
+  if (rp_stride_bh < 0 || max_nnz < 0) return BSATTN_E_SHAPE;
+  const int nqb = T / kBlk, BH = B * H;
+  const int items = BH * nqb;
+  const int gh = group_heads_for(B, H, T);
+  std::vector<int> size(items);
+  int max_size = 0;
+  for (int g = 0; g < items; ++g) {
+    int bh, qb;
+    item_coords(g, BH, nqb, gh, &bh, &qb);
+    int sl = T;
+    if (seq_lens) sl = std::min(seq_lens[bh / H], T);
+    int n = 0;
+    if (qb * kBlk < sl) {
+      const int32_t* rp = row_ptr + static_cast<long long>(bh) * rp_stride_bh + qb;
+      int n_off = std::max(rp[1] - rp[0] - 1, 0);
+      if (n_off > 0 && (rp[0] < 0 || static_cast<long long>(rp[0]) + n_off > max_nnz)) n_off = 0;
+      n = n_off + 1;
+    }
+    size[g] = n;
+    max_size = std::max(max_size, n);
+  }
+  // Counting sort by size, descending and stable.
+  std::vector<int> start(max_size + 2, 0);
+  for (int g = 0; g < items; ++g) ++start[max_size - size[g] + 1];
+  for (int i = 1; i <= max_size + 1; ++i) start[i] += start[i - 1];
+  std::vector<int> order(items);
+  for (int g = 0; g < items; ++g) order[start[max_size - size[g]]++] = g;
+  // Snake deal; CTA c's items keep their sorted order.
+  std::vector<int> cta(items), count(grid, 0);
+  for (int kpos = 0; kpos < items; ++kpos) {
+    const int r = kpos / grid, i = kpos - r * grid;
+    cta[kpos] = (r & 1) ? grid - 1 - i : i;
+    ++count[cta[kpos]];
+  }
+  plan[0] = kPlanMagic;
+  plan[1] = grid;
+  plan[2] = items;
+  plan[3] = 0;
+  int32_t* off = plan + kPlanHeader;
+  int32_t* list = off + grid + 1;
+  off[0] = 0;
+  for (int c = 0; c < grid; ++c) off[c + 1] = off[c] + count[c];
+  std::vector<int> fill(off, off + grid);
+  for (int kpos = 0; kpos < items; ++kpos) list[fill[cta[kpos]]++] = order[kpos];
+  return BSATTN_OK;
 }
 
 int bsattn_check_error(void* workspace, void* stream, int* status) {
