@@ -23,7 +23,8 @@
 //       WG1 (warps 4-7)   softmax for keys 0..63 of every tile   (thread t owns query row t)
 //       WG2 (warps 8-11)  softmax for keys 64..127 of every tile (same rows; the two halves of a
 //                         row exchange their maxima through shared memory)
-//       WG3 (warps 12-15) epilogue: o = O / l, lse, global stores, frees the O buffer
+//       WG3 (warps 12-15) epilogue: o = O / l into a 16 KB 128B-swizzled staging buffer, one TMA
+//                         tensor store per 64-column half, lse, frees the O buffer
 //     The producer and MMA warps have the lowest warp ids: the warp schedulers favour them over
 //     the softmax warps that share their SMSPs, which keeps MMA issue off the critical path.
 //     The producer and MMA warps run their schedules with all 32 lanes so addresses and
@@ -92,6 +93,7 @@ static_assert(kLaunchRegs * kThreads <= 65536, "launch register total");
 struct alignas(1024) SharedStorage {
   uint8_t q[2][kTileBytes];
   uint8_t kv[kStages][kTileBytes];
+  uint8_t ostage[kTileBytes / 2];   // o staging: 128 rows x 64 columns, 128B-swizzled (TMA store)
   float xmax[2][2][kBlk];     // [tile parity][half][row]: partial row maxima
   float stats[2][3][kBlk];    // [item parity]{m, l_half0, l_half1}[row]
   uint64_t q_full[2];
@@ -258,6 +260,17 @@ __device__ __forceinline__ void tile_next(TileIter& x, const FwdParams& p, bool*
   x.j = 0;
   ++x.ii;
   x.valid = seek_active(x, p, csr_bad);
+}
+
+
+// Barrier 1 over the epilogue warpgroup only (128 threads).
+__device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// Same barrier with an OR over the warpgroup: every thread gets true when any thread passed true.
+__device__ __forceinline__ bool epi_any(bool v) {
+  uint32_t r;
+  asm volatile("{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\tbar.red.or.pred b, 1, 128, a;\n\tselp.u32 %0, 1, 0, b;\n\t}"
+               : "=r"(r) : "r"(v ? 1u : 0u) : "memory");
+  return r != 0;
 }
 
 __device__ __forceinline__ void raise_error(const FwdParams& p, int code) {
@@ -683,7 +696,8 @@ __device__ __forceinline__ void store_row32(const FwdParams& p, size_t row, int 
   for (int i = 0; i < 4; ++i) dst[i] = pk[i];
 }
 
-__device__ void epilogue_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem) {
+__device__ void epilogue_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem,
+                              const CUtensorMap* to) {
   const int t = threadIdx.x - kEpiWarp0 * 32;
   const int wq = t >> 5;
   const uint32_t lane_addr = tmem + (static_cast<uint32_t>(wq * 32) << 16);
@@ -705,26 +719,55 @@ __device__ void epilogue_role(SharedStorage& sh, const FwdParams& p, uint32_t tm
     }
     const int ob = ii & 1;
     const uint32_t ph = (static_cast<uint32_t>(ii) >> 1) & 1u;
-    if (!wait_warp(ptx::smem_u32(&sh.o_full[ob]), ph, sh, p)) return;
-    if (!wait_warp(ptx::smem_u32(&sh.stats_rdy[ob]), ph, sh, p)) return;
+    // The four warps take one decision: the named barriers below need all of them.
+    bool ok = wait_warp(ptx::smem_u32(&sh.o_full[ob]), ph, sh, p);
+    if (ok) ok = wait_warp(ptx::smem_u32(&sh.stats_rdy[ob]), ph, sh, p);
+    if (epi_any(!ok)) return;
     ptx::tc_fence_after();
     const bool row_valid = q_pos < it.seq_len;
     const float m_run = sh.stats[ob][0][t];
     const float l_run = sh.stats[ob][1][t] + sh.stats[ob][2][t];
     const float inv_l = l_run > 0.0f ? 1.0f / l_run : 1.0f;
     const uint32_t o_addr = lane_addr + kOCol + ob * 128;
+    const uint32_t stage = ptx::smem_u32(sh.ostage) + static_cast<uint32_t>(t) * 128u;
+    const int row0 = it.bh * p.T + it.qb * kBlk;
 #pragma unroll 1
-    for (int c = 0; c < 4; ++c) {
-      uint32_t orow[32];
-      ptx::tmem_ld32(o_addr + c * 32, orow);
-      ptx::tmem_wait_ld();
-      float of[32];
+    for (int h = 0; h < 2; ++h) {
+      if (t == 0) ptx::bulk_wait_read0();  // the previous store has read the staging buffer
+      epi_sync();
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t orow[32];
+        ptx::tmem_ld32(o_addr + h * 64 + c * 32, orow);
+        ptx::tmem_wait_ld();
+        uint32_t w[16];
 #pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        ptx::reg_fence(orow[i]);
-        of[i] = __uint_as_float(orow[i]);
+        for (int i = 0; i < 16; ++i) {
+          ptx::reg_fence(orow[2 * i]);
+          ptx::reg_fence(orow[2 * i + 1]);
+          const float a = row_valid ? __uint_as_float(orow[2 * i]) * inv_l : 0.0f;
+          const float b = row_valid ? __uint_as_float(orow[2 * i + 1]) * inv_l : 0.0f;
+          if (p.out_bf16) {
+            __nv_bfloat162 v2 = __floats2bfloat162_rn(a, b);
+            w[i] = *reinterpret_cast<uint32_t*>(&v2);
+          } else {
+            __half2 v2 = __floats2half2_rn(a, b);
+            w[i] = *reinterpret_cast<uint32_t*>(&v2);
+          }
+        }
+        // 16-byte chunk k of this row lands at chunk k ^ (row % 8): the 128-byte swizzle.
+#pragma unroll
+        for (int kq = 0; kq < 4; ++kq) {
+          const uint32_t chunk = static_cast<uint32_t>((c * 4 + kq) ^ (t & 7));
+          ptx::sts128(stage + chunk * 16u, w[4 * kq], w[4 * kq + 1], w[4 * kq + 2], w[4 * kq + 3]);
+        }
       }
-      store_row32(p, row, c * 32, of, inv_l, row_valid);
+      ptx::fence_async_smem();
+      epi_sync();
+      if (t == 0) {
+        ptx::tma_store_3d(to, ptx::smem_u32(sh.ostage), 0, row0, h);
+        ptx::bulk_commit();
+      }
     }
     if (p.lse) {
       p.lse[row] = (row_valid && l_run > 0.0f) ? m_run * 0.69314718055994531f + logf(l_run)
@@ -738,7 +781,8 @@ __device__ void epilogue_role(SharedStorage& sh, const FwdParams& p, uint32_t tm
 
 __global__ void __launch_bounds__(kThreads, 1)
     bsattn_fwd_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
-                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ FwdParams p) {
+                      const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap to,
+                      const __grid_constant__ FwdParams p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = ptx::smem_u32(smem_raw);
   SharedStorage& sh =
@@ -774,6 +818,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::tma_prefetch_desc(&tq);
     ptx::tma_prefetch_desc(&tk);
     ptx::tma_prefetch_desc(&tv);
+    ptx::tma_prefetch_desc(&to);
   }
   if (warp == kMmaWarp) {
     ptx::tmem_alloc(ptx::smem_u32(&sh.tmem_base), kTmemCols);
@@ -798,7 +843,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   } else {
     ptx::setmaxnreg_dec<kEpilogueRegs>();
-    epilogue_role(sh, p, tmem);
+    epilogue_role(sh, p, tmem, &to);
+    if (threadIdx.x == kEpiWarp0 * 32) ptx::bulk_wait0();  // every tile store has completed
   }
   __syncwarp();
   // A role that aborted may have left a tensor-memory load or store of its own in flight.
@@ -844,12 +890,13 @@ static EncodeTiledFn get_encode_fn() {
 // strides {256 B per row, 128 B per half}: one box {64, 128, 2} moves a whole 128x128 tile and
 // lands it as two 16 KB blocks (columns 0..63 of all rows, then 64..127), each in the 128-byte
 // swizzled K-major layout the MMA descriptors address.
-static int make_tile_map(CUtensorMap* map, const void* base, uint64_t rows, bool bf16) {
+static int make_tile_map(CUtensorMap* map, const void* base, uint64_t rows, bool bf16,
+                         uint32_t box_z = 2) {
   EncodeTiledFn enc = get_encode_fn();
   if (!enc) return BSATTN_E_TMA;
   cuuint64_t dims[3] = {64, static_cast<cuuint64_t>(rows), 2};
   cuuint64_t strides[2] = {static_cast<cuuint64_t>(kHd * 2), 128};
-  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kBlk), 2};
+  cuuint32_t box[3] = {64, static_cast<cuuint32_t>(kBlk), box_z};
   cuuint32_t estr[3] = {1, 1, 1};
   CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3,
                    const_cast<void*>(base), dims, strides,
@@ -1016,10 +1063,12 @@ int bsattn_fwd_plan(const void* q, const void* k, const void* v, void* o, float*
   int rc = device_setup(&sms);
   if (rc != BSATTN_OK) return rc;
 
-  CUtensorMap tq, tk, tv;
+  CUtensorMap tq, tk, tv, to;
   if ((rc = make_tile_map(&tq, q, rows, qk_bf16)) != BSATTN_OK) return rc;
   if ((rc = make_tile_map(&tk, k, rows, qk_bf16)) != BSATTN_OK) return rc;
   if ((rc = make_tile_map(&tv, v, rows, false)) != BSATTN_OK) return rc;
+  if ((rc = make_tile_map(&to, o, rows, (dtype_flags & BSATTN_OUT_BF16) != 0, 1)) != BSATTN_OK)
+    return rc;
 
   FwdParams p;
   memset(&p, 0, sizeof(p));
@@ -1048,7 +1097,7 @@ int bsattn_fwd_plan(const void* q, const void* k, const void* v, void* o, float*
 
   const int grid = plan != nullptr ? plan_grid : static_cast<int>(std::min<long long>(sms, items));
   bsattn_fwd_kernel<<<grid, kThreads, smem_bytes(), static_cast<cudaStream_t>(stream)>>>(tq, tk,
-                                                                                        tv, p);
+                                                                                        tv, to, p);
   return cudaGetLastError() == cudaSuccess ? BSATTN_OK : BSATTN_E_CUDA;
 }
 
