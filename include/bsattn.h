@@ -169,7 +169,9 @@ BSATTN_API int bsattn_build_csr(int kind, int nqb, int prefix, int window, int n
 /* Human-readable text for a BSATTN_E* code. */
 BSATTN_API const char* bsattn_strerror(int code);
 
-/* ABI version of this header (major*100 + minor). */
+/* ABI version of this header (major*100 + minor): 101.  Minor 1 added dtype flags
+ * (BSATTN_IN_BF16, bsattn_bf16_to_f16), work lists (bsattn_plan, bsattn_fwd_plan, BSATTN_E_PLAN)
+ * and device-built CSR patterns (bsattn_build_csr); every 100 call keeps its meaning. */
 BSATTN_API int bsattn_version(void);
 
 #ifdef __cplusplus

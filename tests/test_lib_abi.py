@@ -40,7 +40,7 @@ def test_library_is_sm100a_only_and_driver_free():
 
 def test_version_workspace_strerror():
     lib = _lib.load()
-    assert lib.bsattn_version() == 100
+    assert lib.bsattn_version() == 101
     assert lib.bsattn_workspace_bytes() >= 4
     for code in range(0, -12, -1):
         assert _lib.strerror(code) != "unknown error"

@@ -997,7 +997,7 @@ extern "C" {
 
 size_t bsattn_workspace_bytes(void) { return kWsInts * sizeof(int); }
 
-int bsattn_version(void) { return 100; }
+int bsattn_version(void) { return 101; }
 
 void bsattn_set_timeout_ns(uint64_t ns) { g_timeout_ns = ns > 0 ? ns : 1; }
 
