@@ -4,10 +4,10 @@ Runs ``block_sparse_attn_fwd`` of sissississi-013/usagi (kernels v4, v7 and v1) 
 ``TRITON_INTERPRET=1`` on CPU tensors -- the reference executing its own code path -- for each
 case in ``cases.py`` and stores the reference's outputs (o as bf16 bit patterns, lse fp32).
 
-This script needs the reference checkout (default /root/reference, or $USAGI_REFERENCE); the
-committed fixtures are what the tests read, so nothing at test time touches the reference.
+This script needs a checkout of the reference, named by $USAGI_REFERENCE; the committed fixtures
+are what the tests read, so nothing at test time touches the reference.
 
-    TRITON_INTERPRET=1 python tests/golden/make_golden.py
+    USAGI_REFERENCE=<reference checkout> TRITON_INTERPRET=1 python tests/golden/make_golden.py
 """
 from __future__ import annotations
 
@@ -25,7 +25,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, HERE)
 import cases  # noqa: E402
 
-REF = os.environ.get("USAGI_REFERENCE", "/root/reference")
+REF = os.environ.get("USAGI_REFERENCE")
+if not REF:
+    raise SystemExit("set USAGI_REFERENCE to the reference checkout")
 KERNELS = {
     "v4": "kernels/v4_leaderboard_0740ms.py",
     "v7": "kernels/v7_blockptr_warpspec.py",

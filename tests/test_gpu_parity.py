@@ -1,7 +1,7 @@
 """Parity of the sm_100a kernel (through the public API / C ABI) against the reference's golden
 outputs and the fp32 CPU oracle, plus size-independent properties at the benchmark sizes.
 
-Tolerances: max |do| <= 1e-2 and mean |do| <= 1e-3 against both the
+Tolerances (the path's contract): max |do| <= 1e-2 and mean |do| <= 1e-3 against both the
 reference Triton kernel (golden fixtures) and the fp32 dense-masked oracle.  A tighter regression
 bound (max 4e-3, mean 2e-4 against the fp32 oracle) guards against silent precision loss: the
 kernel's own error budget is fp16 rounding of P (~2^-11 relative) and of o (half an fp16 ulp).
