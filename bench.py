@@ -235,6 +235,52 @@ def _pattern_flops(fam):
     return _FLOPS_CACHE[fam]
 
 
+# Window families whose rows also have the analytic form of bsattn_fwd_window: (window, global).
+ANALYTIC = {"window8": (8, 0), "prefix4+window4": (4, 4)}
+
+
+def measure_analytic(ub, inputs, outs, lses, flush, device, args):
+    """The window families again, through bsattn_fwd_window (rows from closed forms, no CSR
+    arrays), timed like the headline calls (L2 flushed before each), next to the CSR timing of the
+    same calls; the outputs must equal the CSR outputs bit for bit."""
+    fams = [f for f in FAMILIES if f in ANALYTIC]
+    if not fams:
+        return None
+    plans = {f: ub.make_window_plan(B_PER_RANK, H, T, *ANALYTIC[f], device=device) for f in fams}
+    res = {}
+    for f in fams:
+        q, k, v, rp, ci, plan = inputs[f]
+        o_a = torch.empty_like(outs[f])
+        l_a = torch.empty_like(lses[f])
+        w, g = ANALYTIC[f]
+        runs = {
+            "csr": lambda: ub.block_sparse_attn_fwd(q, k, v, rp, ci, None, out=outs[f],
+                                                    lse_out=lses[f], plan=plan),
+            "analytic": lambda: ub.block_sparse_attn_fwd_window(
+                q, k, v, None, window=w, global_blocks=g, out=o_a, lse_out=l_a, plan=plans[f]),
+        }
+        n = max(10, min(args.steps, 50))
+        ms = {}
+        for name, fn in runs.items():
+            for _ in range(3):
+                flush.zero_()
+                fn()
+            evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                   for _ in range(n)]
+            for a, b in evs:
+                flush.zero_()
+                a.record()
+                fn()
+                b.record()
+            torch.cuda.synchronize()
+            ms[name] = statistics.median(a.elapsed_time(b) for a, b in evs)
+        ub.check_errors(device)
+        assert torch.equal(o_a, outs[f]) and torch.equal(l_a, lses[f])
+        res[f] = {"ms_analytic": ms["analytic"], "ms_csr": ms["csr"], "window": w,
+                  "global_blocks": g, "bitwise_equal_to_csr": True}
+    return res
+
+
 def measure_e2e(ub, inputs, outs, lses, flops_step, device, world, args):
     """Same metric through the public API with host buffers: per step and family, H2D of
     q/k/v/row_ptr/col_idx (and the work list) from pinned memory, the call, D2H of o and lse --
@@ -441,6 +487,11 @@ def main():
     if not args.quick:
         e2e = measure_e2e(ub, inputs, outs, lses, flops_step, device, world, args)
 
+    # ---------------- the window families through the analytic entry point (outside the timing)
+    analytic = None
+    if not args.quick and rank == 0:
+        analytic = measure_analytic(ub, inputs, outs, lses, flush, device, args)
+
     # ---------------- optional gather of o to rank 0 (outside the data path)
     gather_ms = None
     if world > 1 and not args.no_gather:
@@ -489,6 +540,8 @@ def main():
         "traffic_bytes_per_launch" in traffic else None,
         "traffic_note": traffic.get("note") if traffic else None,
     }
+    if analytic is not None:
+        line["analytic_rows"] = analytic
     if gather_ms is not None:
         line["gather_ms"] = gather_ms
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

@@ -102,6 +102,23 @@ BSATTN_API int bsattn_plan(const int32_t* row_ptr, int64_t rp_stride_bh, const i
                            int B, int H, int T, int max_nnz, int grid, int32_t* plan,
                            size_t plan_bytes);
 
+/* Forward pass over analytic rows, with no row_ptr / col_idx: row i of every head lists the
+ * first global_blocks blocks not covered by the window, then blocks max(0, i-window+1) .. i, so
+ * it holds min(i + 1, global_blocks + window) blocks in ascending order, the diagonal last.
+ * Replaces the reference's analytic kernels _fwd_window (global_blocks == 0,
+ * kernels/v1_baseline.py:144-224) and _fwd_window_global (kernels/v1_baseline.py:227-322); the
+ * result is bit-identical to bsattn_fwd_plan with the same rows as CSR (bsattn_build_csr with
+ * BSATTN_CSR_WINDOW / BSATTN_CSR_PREFIX_WINDOW).  window >= 1, global_blocks >= 0.  plan may
+ * come from bsattn_plan_window (or be NULL); the other arguments are those of bsattn_fwd_plan. */
+BSATTN_API int bsattn_fwd_window(const void* q, const void* k, const void* v, void* o, float* lse,
+                                 const int32_t* seq_lens, int B, int H, int T, int D, int window,
+                                 int global_blocks, float scale, int dtype_flags,
+                                 const int32_t* plan, int plan_grid, void* workspace,
+                                 size_t workspace_bytes, void* stream);
+/* Work list for bsattn_fwd_window (seq_lens is a HOST array or NULL). */
+BSATTN_API int bsattn_plan_window(const int32_t* seq_lens, int B, int H, int T, int window,
+                                  int global_blocks, int grid, int32_t* plan, size_t plan_bytes);
+
 /* Allocation-free variant of bsattn_fwd.  No counterpart in the reference: its Python entry
  * point allocated outputs and metadata with torch on every call.
  *
@@ -169,9 +186,10 @@ BSATTN_API int bsattn_build_csr(int kind, int nqb, int prefix, int window, int n
 /* Human-readable text for a BSATTN_E* code. */
 BSATTN_API const char* bsattn_strerror(int code);
 
-/* ABI version of this header (major*100 + minor): 101.  Minor 1 added dtype flags
+/* ABI version of this header (major*100 + minor): 102.  Minor 1 added dtype flags
  * (BSATTN_IN_BF16, bsattn_bf16_to_f16), work lists (bsattn_plan, bsattn_fwd_plan, BSATTN_E_PLAN)
- * and device-built CSR patterns (bsattn_build_csr); every 100 call keeps its meaning. */
+ * and device-built CSR patterns (bsattn_build_csr); minor 2 the analytic window rows
+ * (bsattn_fwd_window, bsattn_plan_window).  Every 100 call keeps its meaning. */
 BSATTN_API int bsattn_version(void);
 
 #ifdef __cplusplus

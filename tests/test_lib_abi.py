@@ -40,7 +40,7 @@ def test_library_is_sm100a_only_and_driver_free():
 
 def test_version_workspace_strerror():
     lib = _lib.load()
-    assert lib.bsattn_version() == 101
+    assert lib.bsattn_version() == 102
     assert lib.bsattn_workspace_bytes() >= 4
     for code in range(0, -12, -1):
         assert _lib.strerror(code) != "unknown error"
@@ -69,6 +69,30 @@ def test_argument_validation_before_device():
     assert _call(q=24) == _lib.E_ALIGN
     assert _call(ws=None) == _lib.E_WORKSPACE
     assert _call(wsb=4) == _lib.E_WORKSPACE
+
+
+def test_window_entry_validation_before_device():
+    lib = _lib.load()
+
+    def call(**kw):
+        a = dict(q=16, sl=None, B=1, H=1, T=128, D=128, window=4, glob=0, od=0, plan=None, pg=0,
+                 ws=16, wsb=256)
+        a.update(kw)
+        return lib.bsattn_fwd_window(a["q"], 16, 16, 16, None, a["sl"], a["B"], a["H"], a["T"],
+                                     a["D"], a["window"], a["glob"], 0.0, a["od"], a["plan"],
+                                     a["pg"], a["ws"], a["wsb"], None)
+
+    assert call(window=0) == _lib.E_SHAPE
+    assert call(window=-3) == _lib.E_SHAPE
+    assert call(glob=-1) == _lib.E_SHAPE
+    assert call(q=None) == _lib.E_NULL
+    assert call(T=200) == _lib.E_SHAPE
+    assert call(D=64) == _lib.E_SHAPE
+    assert call(od=4) == _lib.E_DTYPE
+    assert call(q=24) == _lib.E_ALIGN
+    assert call(wsb=4) == _lib.E_WORKSPACE
+    assert call(plan=16, pg=0) == _lib.E_PLAN
+    assert call(plan=18, pg=1) == _lib.E_PLAN
 
 
 def test_bf16_converter_validation_before_device():

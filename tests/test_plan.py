@@ -90,3 +90,39 @@ def test_plan_argument_errors():
     assert lib.bsattn_plan(rp.data_ptr(), 0, None, 1, 1, 256, 2, 2, small.data_ptr(),
                            16) == _lib.E_WORKSPACE
     assert lib.bsattn_plan(None, 0, None, 1, 1, 256, 2, 2, small.data_ptr(), 16) == _lib.E_NULL
+
+
+def _window_plan(B, H, T, window, global_blocks, grid, seq_lens=None):
+    lib = _lib.load()
+    nb = ctypes.c_size_t(0)
+    assert lib.bsattn_plan_bytes(B, H, T, grid, ctypes.byref(nb)) == 0
+    buf = torch.empty(nb.value // 4, dtype=torch.int32)
+    sl = None if seq_lens is None else seq_lens.to(torch.int32).contiguous()
+    rc = lib.bsattn_plan_window(sl.data_ptr() if sl is not None else None, B, H, T, window,
+                                global_blocks, grid, buf.data_ptr(), nb.value)
+    assert rc == 0, _lib.strerror(rc)
+    return buf
+
+
+@pytest.mark.parametrize("window,global_blocks", [(8, 0), (4, 4), (1, 0), (16, 8), (3, 1)])
+def test_window_plan_equals_csr_plan(window, global_blocks):
+    """Analytic rows and the same rows as CSR give the same work list, entry for entry."""
+    B, H, T = 2, 3, 4096
+    for sl in (None, torch.tensor([1000, 4096])):
+        if global_blocks:
+            pat = P.prefix_window_pattern(B, H, T, global_blocks, window)
+        else:
+            pat = P.window_pattern(B, H, T, window)
+        for grid in (148, 37):
+            assert torch.equal(_window_plan(B, H, T, window, global_blocks, grid, sl),
+                               _plan(pat, B, H, T, grid, sl))
+
+
+def test_window_plan_argument_errors():
+    lib = _lib.load()
+    buf = torch.empty(64, dtype=torch.int32)
+    assert lib.bsattn_plan_window(None, 1, 1, 256, 0, 0, 2, buf.data_ptr(), 256) == _lib.E_SHAPE
+    assert lib.bsattn_plan_window(None, 1, 1, 256, 4, -1, 2, buf.data_ptr(), 256) == _lib.E_SHAPE
+    assert lib.bsattn_plan_window(None, 1, 1, 256, 4, 0, 2, None, 256) == _lib.E_NULL
+    assert lib.bsattn_plan_window(None, 1, 1, 256, 4, 0, 2, buf.data_ptr(), 8) == _lib.E_WORKSPACE
+    assert lib.bsattn_plan_window(None, 1, 1, 256, 4, 0, 2, buf.data_ptr(), 256) == _lib.OK

@@ -9,7 +9,9 @@ from .api import (  # noqa: F401
     BsattnError,
     Plan,
     block_sparse_attn_fwd,
+    block_sparse_attn_fwd_window,
     make_plan,
+    make_window_plan,
     check_errors,
     set_timeout_ns,
     setup,

@@ -40,6 +40,17 @@ SIGNATURES = {
         _c_void_p, _c_int,                        # plan (device), plan_grid
         _c_void_p, _c_size_t, _c_void_p,          # workspace, bytes, stream
     ]),
+    "bsattn_fwd_window": (_c_int, [
+        _c_void_p, _c_void_p, _c_void_p,          # q, k, v
+        _c_void_p, _c_void_p, _c_void_p,          # o, lse, seq_lens
+        _c_int, _c_int, _c_int, _c_int,           # B, H, T, D
+        _c_int, _c_int,                           # window, global_blocks
+        ctypes.c_float, _c_int,                   # scale, dtype_flags
+        _c_void_p, _c_int,                        # plan (device), plan_grid
+        _c_void_p, _c_size_t, _c_void_p,          # workspace, bytes, stream
+    ]),
+    "bsattn_plan_window": (_c_int, [_c_void_p, _c_int, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                    _c_void_p, _c_size_t]),
     "bsattn_plan_bytes": (_c_int, [_c_int, _c_int, _c_int, _c_int, ctypes.POINTER(_c_size_t)]),
     "bsattn_plan": (_c_int, [_c_void_p, ctypes.c_int64, _c_void_p, _c_int, _c_int, _c_int, _c_int,
                              _c_int, _c_void_p, _c_size_t]),

@@ -39,6 +39,8 @@ __all__ = [
     "set_timeout_ns",
     "Plan",
     "make_plan",
+    "block_sparse_attn_fwd_window",
+    "make_window_plan",
 ]
 
 BLOCK_SIZE = 128
@@ -139,11 +141,28 @@ def make_plan(row_ptr: torch.Tensor, col_idx: torch.Tensor, B: int, H: int, T: i
               grid: Optional[int] = None) -> Plan:
     """Build a :class:`Plan` on the host from the pattern (copied to the host once) and move it
     to ``device``.  ``grid`` defaults to the persistent grid of the call: one CTA per SM."""
+    lib = _lib.load()
+    rp, rp_stride = _bh_view(row_ptr.detach().cpu(), B, H, "row_ptr")
+    max_nnz = int(col_idx.shape[-1])
+    return _build_plan(B, H, T, seq_lens, device, grid, "bsattn_plan",
+                       lambda sl, g, buf, n: lib.bsattn_plan(rp.data_ptr(), rp_stride, sl, B, H, T,
+                                                             max_nnz, g, buf, n))
+
+
+def make_window_plan(B: int, H: int, T: int, window: int, global_blocks: int = 0,
+                     seq_lens: Optional[torch.Tensor] = None, device="cuda",
+                     grid: Optional[int] = None) -> Plan:
+    """:class:`Plan` for :func:`block_sparse_attn_fwd_window` (``bsattn_plan_window``)."""
+    lib = _lib.load()
+    return _build_plan(B, H, T, seq_lens, device, grid, "bsattn_plan_window",
+                       lambda sl, g, buf, n: lib.bsattn_plan_window(sl, B, H, T, int(window),
+                                                                    int(global_blocks), g, buf, n))
+
+
+def _build_plan(B, H, T, seq_lens, device, grid, name, fill) -> Plan:
     import ctypes
     lib = _lib.load()
     nqb = T // BLOCK_SIZE
-    rp, rp_stride = _bh_view(row_ptr.detach().cpu(), B, H, "row_ptr")
-    max_nnz = int(col_idx.shape[-1])
     sl = None
     if seq_lens is not None:
         sl = seq_lens.detach().cpu().to(torch.int32).contiguous()
@@ -155,31 +174,14 @@ def make_plan(row_ptr: torch.Tensor, col_idx: torch.Tensor, B: int, H: int, T: i
     if rc != 0:
         raise BsattnError(rc, "bsattn_plan_bytes")
     host = torch.empty(nbytes.value // 4, dtype=torch.int32)
-    rc = lib.bsattn_plan(rp.data_ptr(), rp_stride, sl.data_ptr() if sl is not None else None,
-                         B, H, T, max_nnz, grid, host.data_ptr(), nbytes.value)
+    rc = fill(sl.data_ptr() if sl is not None else None, grid, host.data_ptr(), nbytes.value)
     if rc != 0:
-        raise BsattnError(rc, "bsattn_plan")
+        raise BsattnError(rc, name)
     return Plan(host.to(dev), grid, B, H, T)
 
 
-def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
-                          row_ptr: torch.Tensor, col_idx: torch.Tensor,
-                          seq_lens: Optional[torch.Tensor] = None, *,
-                          scale: Optional[float] = None,
-                          out_dtype: Optional[torch.dtype] = None,
-                          out: Optional[torch.Tensor] = None,
-                          lse_out: Optional[torch.Tensor] = None,
-                          return_lse: bool = True,
-                          plan: Optional[Plan] = None):
-    """Block-sparse causal attention forward on a B200.
-
-    q, k: fp16 or bf16 [B, H, T, 128] CUDA tensors of one dtype, T % 128 == 0; v: the same shape,
-    fp16 or the dtype of q.  row_ptr: int [B, H, T/128 + 1]; col_idx: int [B, H, max_nnz] (or
-    [B*H, .], or one shared [.] row); seq_lens: int [B] or None.  Returns ``(o, lse)`` like the
-    reference (v4 :179): o [B, H, T, 128] in ``out_dtype`` (default: q's dtype), lse fp32
-    [B, H, T] (None if ``return_lse=False``).  ``plan`` (from :func:`make_plan` for this pattern)
-    balances the work across the persistent CTAs; results are identical with or without it.
-    """
+def _prepare(q, k, v, seq_lens, out_dtype, out, lse_out, return_lse):
+    """Shared checks and buffers of the entry points: (q, k, v, flags, seq_lens, o, lse)."""
     lib = _lib.load()
     if q.dim() != 4:
         raise ValueError(f"q must be [B, H, T, D], got {tuple(q.shape)}")
@@ -209,12 +211,6 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         if rc != 0:
             raise BsattnError(rc, "bsattn_bf16_to_f16")
         v = v16
-    nqb = T // BLOCK_SIZE
-    rp, rp_stride = _bh_view(row_ptr.to(dev), B, H, "row_ptr")
-    ci, ci_stride = _bh_view(col_idx.to(dev), B, H, "col_idx")
-    if rp.shape[-1] != nqb + 1:
-        raise ValueError(f"row_ptr: expected last dim {nqb + 1}, got {rp.shape[-1]}")
-    max_nnz = int(ci.shape[-1])
     sl = None
     if seq_lens is not None:
         sl = seq_lens.to(device=dev, dtype=torch.int32).contiguous()
@@ -233,23 +229,93 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
                     or not lse_out.is_contiguous():
                 raise ValueError("lse_out has the wrong shape, dtype or layout")
             lse = lse_out
+    return q, k, v, flags, sl, out, lse
+
+
+def _plan_args(plan, B, H, T, dev):
+    if plan is None:
+        return None, 0
+    if (plan.B, plan.H, plan.T) != (B, H, T) or plan.tensor.device != dev:
+        raise ValueError("plan was built for another shape or device")
+    return plan.tensor.data_ptr(), plan.grid
+
+
+def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                          row_ptr: torch.Tensor, col_idx: torch.Tensor,
+                          seq_lens: Optional[torch.Tensor] = None, *,
+                          scale: Optional[float] = None,
+                          out_dtype: Optional[torch.dtype] = None,
+                          out: Optional[torch.Tensor] = None,
+                          lse_out: Optional[torch.Tensor] = None,
+                          return_lse: bool = True,
+                          plan: Optional[Plan] = None):
+    """Block-sparse causal attention forward on a B200.
+
+    q, k: fp16 or bf16 [B, H, T, 128] CUDA tensors of one dtype, T % 128 == 0; v: the same shape,
+    fp16 or the dtype of q.  row_ptr: int [B, H, T/128 + 1]; col_idx: int [B, H, max_nnz] (or
+    [B*H, .], or one shared [.] row); seq_lens: int [B] or None.  Returns ``(o, lse)`` like the
+    reference (v4 :179): o [B, H, T, 128] in ``out_dtype`` (default: q's dtype), lse fp32
+    [B, H, T] (None if ``return_lse=False``).  ``plan`` (from :func:`make_plan` for this pattern)
+    balances the work across the persistent CTAs; results are identical with or without it.
+    """
+    lib = _lib.load()
+    q, k, v, flags, sl, out, lse = _prepare(q, k, v, seq_lens, out_dtype, out, lse_out,
+                                            return_lse)
+    B, H, T, D = q.shape
+    dev = q.device
+    nqb = T // BLOCK_SIZE
+    rp, rp_stride = _bh_view(row_ptr.to(dev), B, H, "row_ptr")
+    ci, ci_stride = _bh_view(col_idx.to(dev), B, H, "col_idx")
+    if rp.shape[-1] != nqb + 1:
+        raise ValueError(f"row_ptr: expected last dim {nqb + 1}, got {rp.shape[-1]}")
+    max_nnz = int(ci.shape[-1])
     with torch.cuda.device(dev):
         stream = torch.cuda.current_stream(dev).cuda_stream
         ws = _workspace(dev, stream)
-        if plan is not None:
-            if (plan.B, plan.H, plan.T) != (B, H, T) or plan.tensor.device != dev:
-                raise ValueError("plan was built for another shape or device")
+        plan_ptr, plan_grid = _plan_args(plan, B, H, T, dev)
         rc = lib.bsattn_fwd_plan(
             q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
             lse.data_ptr() if lse is not None else None,
             rp.data_ptr(), ci.data_ptr(), sl.data_ptr() if sl is not None else None,
             B, H, T, D, rp_stride, ci_stride, max_nnz,
-            float(scale) if scale is not None else 0.0, flags,
-            plan.tensor.data_ptr() if plan is not None else None,
-            plan.grid if plan is not None else 0,
+            float(scale) if scale is not None else 0.0, flags, plan_ptr, plan_grid,
             ws.data_ptr(), ws.numel() * 4, stream)
     if rc != 0:
         raise BsattnError(rc, "bsattn_fwd")
+    return out, lse
+
+
+def block_sparse_attn_fwd_window(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                                 seq_lens: Optional[torch.Tensor] = None, *, window: int,
+                                 global_blocks: int = 0, scale: Optional[float] = None,
+                                 out_dtype: Optional[torch.dtype] = None,
+                                 out: Optional[torch.Tensor] = None,
+                                 lse_out: Optional[torch.Tensor] = None,
+                                 return_lse: bool = True, plan: Optional[Plan] = None):
+    """Attention over analytic rows, with no CSR tensors (``bsattn_fwd_window``).
+
+    Row i of every head lists the first ``global_blocks`` blocks not covered by the window, then
+    blocks max(0, i - window + 1) .. i: the reference's analytic kernels ``_fwd_window`` and
+    ``_fwd_window_global`` (kernels/v1_baseline.py:144, :227).  Same result, bit for bit, as
+    :func:`block_sparse_attn_fwd` given those rows as CSR; the other arguments are the same.
+    """
+    lib = _lib.load()
+    q, k, v, flags, sl, out, lse = _prepare(q, k, v, seq_lens, out_dtype, out, lse_out,
+                                            return_lse)
+    B, H, T, D = q.shape
+    dev = q.device
+    with torch.cuda.device(dev):
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        ws = _workspace(dev, stream)
+        plan_ptr, plan_grid = _plan_args(plan, B, H, T, dev)
+        rc = lib.bsattn_fwd_window(
+            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+            lse.data_ptr() if lse is not None else None, sl.data_ptr() if sl is not None else None,
+            B, H, T, D, int(window), int(global_blocks),
+            float(scale) if scale is not None else 0.0, flags, plan_ptr, plan_grid,
+            ws.data_ptr(), ws.numel() * 4, stream)
+    if rc != 0:
+        raise BsattnError(rc, "bsattn_fwd_window")
     return out, lse
 
 

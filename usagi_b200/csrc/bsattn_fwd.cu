@@ -132,6 +132,9 @@ struct FwdParams {
   unsigned long long timeout_ns;
   int test_unsignalled_wait;  // test hook: the QK^T issuer first waits on a barrier nobody signals
   const int32_t* plan;        // optional work list built by bsattn_plan (null: round robin)
+  // Analytic rows (window > 0; row_ptr and col_idx unused): row i lists the first `prefix` blocks
+  // not covered by the window, then blocks max(0, i - window + 1) .. i.
+  int window, prefix;
 };
 
 // One work item = one (head, query block).
@@ -156,7 +159,10 @@ __device__ __forceinline__ Item load_item(const FwdParams& p, int g, bool* csr_b
   it.seq_len = sl;
   it.n_steps = 0;
   it.row_start = 0;
-  if (it.qb * kBlk < sl) {
+  if (it.qb * kBlk < sl && p.window > 0) {
+    // min(i + 1, prefix + window) blocks: rows up to prefix + window - 1 are all of 0 .. i.
+    it.n_steps = min(it.qb + 1, p.prefix + p.window);
+  } else if (it.qb * kBlk < sl) {
     const int32_t* rp = p.row_ptr + (long long)it.bh * p.rp_stride + it.qb;
     const int rs = __ldg(rp);
     const int re = __ldg(rp + 1);
@@ -169,6 +175,22 @@ __device__ __forceinline__ Item load_item(const FwdParams& p, int g, bool* csr_b
     it.n_steps = n_off + 1;  // + the diagonal, always computed (v4 :107)
   }
   return it;
+}
+
+// Key block of step j < n_steps - 1 (an off-diagonal block) of item it.  CSR rows read
+// col_idx (v4 :86); an entry out of range sets *csr_bad and is replaced by the diagonal.  Analytic
+// rows have a closed form: with n = n_steps, steps j < n - window are prefix blocks j (the global
+// phase of the reference's analytic kernel, v1_baseline.py:264-265), the rest the window blocks
+// i - (n - 1 - j) (v1_baseline.py:180-181, :282-283).
+__device__ __forceinline__ int offdiag_block(const FwdParams& p, const Item& it, int j,
+                                             bool* csr_bad) {
+  if (p.window > 0) return j < it.n_steps - p.window ? j : it.qb - (it.n_steps - 1 - j);
+  int kb = __ldg(p.col_idx + (long long)it.bh * p.ci_stride + it.row_start + j);
+  if (kb < 0 || kb >= p.nqb) {
+    if (csr_bad) *csr_bad = true;
+    kb = it.qb;
+  }
+  return kb;
 }
 
 // The items of this CTA, in processing order.  Without a work list CTA b takes items b, b + grid,
@@ -381,25 +403,14 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
       q_last_parity = (q_last_parity & ~(1u << b)) | (ph << b);
     }
     int kb = x.it.qb;  // diagonal
-    if (x.j < x.it.n_steps - 1) {
-      kb = __ldg(p.col_idx + (long long)x.it.bh * p.ci_stride + x.it.row_start + x.j);
-      if (kb < 0 || kb >= p.nqb) {
-        csr_bad = true;
-        kb = x.it.qb;
-      }
-    }
+    if (x.j < x.it.n_steps - 1) kb = offdiag_block(p, x.it, x.j, &csr_bad);
     x.kb = kb;
     return load_tile(tk, head_row0 + kb * kBlk);
   };
 
-  // vs trails ks by two tiles; its key block is read again from col_idx (an L1 hit).
+  // vs trails ks by two tiles; its key block is looked up again (for CSR rows an L1 hit).
   auto key_block = [&](const TileIter& x) -> int {
-    int kb = x.it.qb;
-    if (x.j < x.it.n_steps - 1) {
-      kb = __ldg(p.col_idx + (long long)x.it.bh * p.ci_stride + x.it.row_start + x.j);
-      if (kb < 0 || kb >= p.nqb) kb = x.it.qb;
-    }
-    return kb;
+    return x.j < x.it.n_steps - 1 ? offdiag_block(p, x.it, x.j, nullptr) : x.it.qb;
   };
   tile_begin(ks, p, &csr_bad);
   tile_begin(vs, p, nullptr);
@@ -997,7 +1008,7 @@ extern "C" {
 
 size_t bsattn_workspace_bytes(void) { return kWsInts * sizeof(int); }
 
-int bsattn_version(void) { return 101; }
+int bsattn_version(void) { return 102; }
 
 void bsattn_set_timeout_ns(uint64_t ns) { g_timeout_ns = ns > 0 ? ns : 1; }
 
@@ -1039,14 +1050,26 @@ const char* bsattn_strerror(int code) {
   }
 }
 
-int bsattn_fwd_plan(const void* q, const void* k, const void* v, void* o, float* lse,
-                    const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens,
-                    int B, int H, int T, int D, int64_t rp_stride_bh, int64_t ci_stride_bh,
-                    int max_nnz, float scale, int dtype_flags, const int32_t* plan, int plan_grid,
-                    void* workspace, size_t workspace_bytes, void* stream) {
-  if (!q || !k || !v || !o || !row_ptr || !col_idx) return BSATTN_E_NULL;
+}  // extern "C"
+
+namespace bsattn {
+
+// The row pattern of one call: CSR arrays, or analytic prefix + window rows (window > 0).
+struct Pattern {
+  const int32_t* row_ptr;
+  const int32_t* col_idx;
+  int64_t rp_stride, ci_stride;
+  int max_nnz;
+  int window, prefix;
+};
+
+// Checks and launch shared by the CSR and the analytic entry points.
+static int launch_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
+                      const Pattern& pat, const int32_t* seq_lens, int B, int H, int T, int D,
+                      float scale, int dtype_flags, const int32_t* plan, int plan_grid,
+                      void* workspace, size_t workspace_bytes, void* stream) {
+  if (!q || !k || !v || !o) return BSATTN_E_NULL;
   if (B < 1 || H < 1 || T < kBlk || (T % kBlk) != 0 || D != kHd) return BSATTN_E_SHAPE;
-  if (max_nnz < 0 || rp_stride_bh < 0 || ci_stride_bh < 0) return BSATTN_E_SHAPE;
   const long long rows = static_cast<long long>(B) * H * T;
   const long long items = static_cast<long long>(B) * H * (T / kBlk);
   if (rows >= (1ll << 31) || items >= (1ll << 30)) return BSATTN_E_SHAPE;
@@ -1072,15 +1095,17 @@ int bsattn_fwd_plan(const void* q, const void* k, const void* v, void* o, float*
 
   FwdParams p;
   memset(&p, 0, sizeof(p));
-  p.row_ptr = row_ptr;
-  p.col_idx = col_idx;
+  p.row_ptr = pat.row_ptr;
+  p.col_idx = pat.col_idx;
   p.seq_lens = seq_lens;
   p.o = o;
   p.lse = lse;
   p.ws = static_cast<int*>(workspace);
-  p.rp_stride = rp_stride_bh;
-  p.ci_stride = ci_stride_bh;
-  p.max_nnz = max_nnz;
+  p.rp_stride = pat.rp_stride;
+  p.ci_stride = pat.ci_stride;
+  p.max_nnz = pat.max_nnz;
+  p.window = pat.window;
+  p.prefix = pat.prefix;
   p.BH = B * H;
   p.H = H;
   p.T = T;
@@ -1099,6 +1124,42 @@ int bsattn_fwd_plan(const void* q, const void* k, const void* v, void* o, float*
   bsattn_fwd_kernel<<<grid, kThreads, smem_bytes(), static_cast<cudaStream_t>(stream)>>>(tq, tk,
                                                                                         tv, to, p);
   return cudaGetLastError() == cudaSuccess ? BSATTN_OK : BSATTN_E_CUDA;
+}
+
+// Largest window / prefix the analytic rows accept (their sum stays far from int overflow).
+constexpr int kMaxWindow = 1 << 24;
+
+static int check_window(int window, int global_blocks) {
+  if (window < 1 || window > kMaxWindow || global_blocks < 0 || global_blocks > kMaxWindow)
+    return BSATTN_E_SHAPE;
+  return BSATTN_OK;
+}
+
+}  // namespace bsattn
+
+extern "C" {
+
+int bsattn_fwd_plan(const void* q, const void* k, const void* v, void* o, float* lse,
+                    const int32_t* row_ptr, const int32_t* col_idx, const int32_t* seq_lens,
+                    int B, int H, int T, int D, int64_t rp_stride_bh, int64_t ci_stride_bh,
+                    int max_nnz, float scale, int dtype_flags, const int32_t* plan, int plan_grid,
+                    void* workspace, size_t workspace_bytes, void* stream) {
+  if (!row_ptr || !col_idx) return BSATTN_E_NULL;
+  if (max_nnz < 0 || rp_stride_bh < 0 || ci_stride_bh < 0) return BSATTN_E_SHAPE;
+  const Pattern pat{row_ptr, col_idx, rp_stride_bh, ci_stride_bh, max_nnz, 0, 0};
+  return launch_fwd(q, k, v, o, lse, pat, seq_lens, B, H, T, D, scale, dtype_flags, plan,
+                    plan_grid, workspace, workspace_bytes, stream);
+}
+
+int bsattn_fwd_window(const void* q, const void* k, const void* v, void* o, float* lse,
+                      const int32_t* seq_lens, int B, int H, int T, int D, int window,
+                      int global_blocks, float scale, int dtype_flags, const int32_t* plan,
+                      int plan_grid, void* workspace, size_t workspace_bytes, void* stream) {
+  const int rc = check_window(window, global_blocks);
+  if (rc != BSATTN_OK) return rc;
+  const Pattern pat{nullptr, nullptr, 0, 0, 0, window, global_blocks};
+  return launch_fwd(q, k, v, o, lse, pat, seq_lens, B, H, T, D, scale, dtype_flags, plan,
+                    plan_grid, workspace, workspace_bytes, stream);
 }
 
 int bsattn_fwd(const void* q, const void* k, const void* v, void* o, float* lse,
@@ -1120,19 +1181,22 @@ int bsattn_plan_bytes(int B, int H, int T, int grid, size_t* bytes) {
   return BSATTN_OK;
 }
 
+}  // extern "C"
+
+namespace bsattn {
+
 // Work list: items sorted by their tile count, largest first (ties keep the kernel's item order,
 // so the big items stay grouped by head for L2 reuse), dealt to the CTAs in a snake order
-// (0 .. grid-1, then grid-1 .. 0, ...).  Each CTA keeps its items in that sorted order.  The tile
-// count of an item is the kernel's: 0 past seq_len, else the listed off-diagonal blocks plus the
-// diagonal (rows whose range does not fit col_idx count as the diagonal alone, as in load_item).
-int bsattn_plan(const int32_t* row_ptr, int64_t rp_stride_bh, const int32_t* seq_lens, int B,
-                int H, int T, int max_nnz, int grid, int32_t* plan, size_t plan_bytes) {
-  if (!row_ptr || !plan) return BSATTN_E_NULL;
+// (0 .. grid-1, then grid-1 .. 0, ...).  Each CTA keeps its items in that sorted order.
+// row_tiles(bh, qb) is the tile count of a live item (query block below seq_len).
+template <class RowTiles>
+static int build_plan(const int32_t* seq_lens, int B, int H, int T, int grid, int32_t* plan,
+                      size_t plan_bytes, RowTiles row_tiles) {
+  if (!plan) return BSATTN_E_NULL;
   size_t need = 0;
   int rc = bsattn_plan_bytes(B, H, T, grid, &need);
   if (rc != BSATTN_OK) return rc;
   if (plan_bytes < need) return BSATTN_E_WORKSPACE;
-  if (rp_stride_bh < 0 || max_nnz < 0) return BSATTN_E_SHAPE;
   const int nqb = T / kBlk, BH = B * H;
   const int items = BH * nqb;
   const int gh = group_heads_for(B, H, T);
@@ -1143,13 +1207,7 @@ int bsattn_plan(const int32_t* row_ptr, int64_t rp_stride_bh, const int32_t* seq
     item_coords(g, BH, nqb, gh, &bh, &qb);
     int sl = T;
     if (seq_lens) sl = std::min(seq_lens[bh / H], T);
-    int n = 0;
-    if (qb * kBlk < sl) {
-      const int32_t* rp = row_ptr + static_cast<long long>(bh) * rp_stride_bh + qb;
-      int n_off = std::max(rp[1] - rp[0] - 1, 0);
-      if (n_off > 0 && (rp[0] < 0 || static_cast<long long>(rp[0]) + n_off > max_nnz)) n_off = 0;
-      n = n_off + 1;
-    }
+    const int n = qb * kBlk < sl ? row_tiles(bh, qb) : 0;
     size[g] = n;
     max_size = std::max(max_size, n);
   }
@@ -1177,6 +1235,34 @@ int bsattn_plan(const int32_t* row_ptr, int64_t rp_stride_bh, const int32_t* seq
   std::vector<int> fill(off, off + grid);
   for (int kpos = 0; kpos < items; ++kpos) list[fill[cta[kpos]]++] = order[kpos];
   return BSATTN_OK;
+}
+
+}  // namespace bsattn
+
+extern "C" {
+
+// The tile count of a CSR item is the kernel's: the listed off-diagonal blocks plus the diagonal
+// (rows whose range does not fit col_idx count as the diagonal alone, as in load_item).
+int bsattn_plan(const int32_t* row_ptr, int64_t rp_stride_bh, const int32_t* seq_lens, int B,
+                int H, int T, int max_nnz, int grid, int32_t* plan, size_t plan_bytes) {
+  if (!row_ptr) return BSATTN_E_NULL;
+  if (rp_stride_bh < 0 || max_nnz < 0) return BSATTN_E_SHAPE;
+  return build_plan(seq_lens, B, H, T, grid, plan, plan_bytes, [&](int bh, int qb) {
+    const int32_t* rp = row_ptr + static_cast<long long>(bh) * rp_stride_bh + qb;
+    int n_off = std::max(rp[1] - rp[0] - 1, 0);
+    if (n_off > 0 && (rp[0] < 0 || static_cast<long long>(rp[0]) + n_off > max_nnz)) n_off = 0;
+    return n_off + 1;
+  });
+}
+
+// Analytic rows hold min(qb + 1, global_blocks + window) tiles.
+int bsattn_plan_window(const int32_t* seq_lens, int B, int H, int T, int window, int global_blocks,
+                       int grid, int32_t* plan, size_t plan_bytes) {
+  const int rc = check_window(window, global_blocks);
+  if (rc != BSATTN_OK) return rc;
+  const int L = window + global_blocks;
+  return build_plan(seq_lens, B, H, T, grid, plan, plan_bytes,
+                    [&](int, int qb) { return std::min(qb + 1, L); });
 }
 
 int bsattn_check_error(void* workspace, void* stream, int* status) {
