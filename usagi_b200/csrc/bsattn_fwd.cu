@@ -76,6 +76,10 @@ constexpr int kPolyEvery = 4;              // every 4th pair of exponentials run
 // finish within microseconds, and the CTA must not exit (or free tensor memory) before they do.
 constexpr unsigned long long kDrainNs = 100000000ull;
 constexpr int kWsInts = 64;                // workspace: int32[64]
+// Active-item ring: the producer publishes each active item's descriptor once; the softmax
+// warpgroups, both MMA issuers and the producer's V stream read it from shared memory.
+constexpr int kItemRing = 8;
+constexpr int kItemReaders = 256 + 3;      // softmax threads, S issuer, PV issuer, V stream
 constexpr uint32_t kIdescQK = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/false);
 constexpr uint32_t kIdescQKBf16 = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/false, true);
 constexpr uint32_t kIdescPV = ptx::idesc_f16_f32(128, 128, /*b_mn_major=*/true);
@@ -89,6 +93,12 @@ constexpr uint32_t kEpilogueRegs = 88;
 static_assert(2 * kSoftmaxRegs + kControlRegs + kEpilogueRegs <= 4 * kLaunchRegs,
               "register split exceeds the launch allocation");
 static_assert(kLaunchRegs * kThreads <= 65536, "launch register total");
+
+// One work item = one (head, query block).  n_steps = 0: inactive (past seq_len); in the
+// active-item ring it marks the end of the CTA's items.
+struct Item {
+  int bh, qb, seq_len, n_steps, row_start;
+};
 
 struct alignas(1024) SharedStorage {
   uint8_t q[2][kTileBytes];
@@ -107,6 +117,9 @@ struct alignas(1024) SharedStorage {
   uint64_t o_full[2];         // O[b] holds a finished item
   uint64_t o_free[2];         // epilogue done reading O[b] and its stats
   uint64_t stats_rdy[2];      // softmax published stats[b]
+  Item items[kItemRing];      // [active item % kItemRing]
+  uint64_t item_full[kItemRing];
+  uint64_t item_empty[kItemRing];
   uint64_t drain;
   uint64_t unsignalled;       // never arrived on; waited on only by the test hook
   uint32_t tmem_base;
@@ -137,10 +150,6 @@ struct FwdParams {
   int window, prefix;
 };
 
-// One work item = one (head, query block).
-struct Item {
-  int bh, qb, seq_len, n_steps, row_start;
-};
 
 // Item order: heads are taken in groups of group_heads (sized on the host so a group's K and V fit
 // in L2 with room to spare); inside a group, bands of decreasing qb (longest causal rows first),
@@ -349,6 +358,56 @@ __device__ __forceinline__ void wait_drain(uint32_t bar, uint32_t parity, const 
   }
 }
 
+// Active-item ring.  The producer's K stream, which reaches every item first, writes the
+// descriptor of each active item once (and an n_steps = 0 end marker after the last); the other
+// item walkers read it from shared memory instead of reloading the work list, row_ptr and
+// seq_lens at every item boundary.  Slot k % kItemRing; item_full completes once per write,
+// item_empty once all kItemReaders have read the slot.  The producer leads every reader by at
+// most a few tiles (its K/V ring holds four stages) and every active item has at least one tile,
+// so a write never waits for a reader that is kItemRing items behind.
+__device__ __forceinline__ bool ring_write(SharedStorage& sh, const FwdParams& p, int k,
+                                           const Item& it) {
+  const int slot = k & (kItemRing - 1);
+  if (k >= kItemRing &&
+      !wait_ctl(ptx::smem_u32(&sh.item_empty[slot]),
+                static_cast<uint32_t>(k / kItemRing + 1) & 1u, sh, p))
+    return false;
+  sh.items[slot] = it;
+  ptx::mbar_arrive(ptx::smem_u32(&sh.item_full[slot]));
+  return true;
+}
+
+// One reader thread: active item k (false when this CTA aborted).
+__device__ __forceinline__ bool ring_read(SharedStorage& sh, const FwdParams& p, int k, Item& it) {
+  const int slot = k & (kItemRing - 1);
+  if (!wait_ctl(ptx::smem_u32(&sh.item_full[slot]), static_cast<uint32_t>(k / kItemRing) & 1u, sh,
+                p))
+    return false;
+  it = sh.items[slot];
+  ptx::mbar_arrive(ptx::smem_u32(&sh.item_empty[slot]));
+  return true;
+}
+
+// TileIter walks over the ring (for the readers).
+__device__ __forceinline__ void ring_tile_begin(TileIter& x, SharedStorage& sh,
+                                                const FwdParams& p) {
+  x.ii = 0;
+  x.j = 0;
+  x.t = 0;
+  x.valid = ring_read(sh, p, 0, x.it) && x.it.n_steps > 0;
+}
+
+__device__ __forceinline__ void ring_tile_next(TileIter& x, SharedStorage& sh, const FwdParams& p) {
+  ++x.t;
+  if (x.j + 1 < x.it.n_steps) {
+    ++x.j;
+    return;
+  }
+  x.j = 0;
+  ++x.ii;
+  x.valid = ring_read(sh, p, x.ii, x.it) && x.it.n_steps > 0;
+}
+
 // ------------------------------------------------------------------------------------------
 // Producer warp.  Load order = MMA consumption order: K(0), K(1), then V(t), K(t+2) for
 // t = 0, 1, ...; Q of an item right before its first K.  Lane 0 issues the copies.
@@ -412,11 +471,29 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
   auto key_block = [&](const TileIter& x) -> int {
     return x.j < x.it.n_steps - 1 ? offdiag_block(p, x.it, x.j, nullptr) : x.it.qb;
   };
+  // ks publishes each new active item (and the end marker) to the item ring.
+  int published = 0;
+  auto publish = [&]() -> bool {
+    if (ks.valid) {
+      if (ks.j != 0 || ks.ii < published) return true;
+      published = ks.ii + 1;
+      return ring_write(sh, p, ks.ii, ks.it);
+    }
+    if (published > ks.ii) return true;  // end marker already written
+    published = ks.ii + 1;
+    Item end;
+    end.bh = end.qb = end.seq_len = end.row_start = 0;
+    end.n_steps = 0;
+    return ring_write(sh, p, ks.ii, end);
+  };
   tile_begin(ks, p, &csr_bad);
-  tile_begin(vs, p, nullptr);
+  ok = publish();
+  if (ok) ring_tile_begin(vs, sh, p);
+  else vs.valid = false;
   for (int i = 0; i < 2 && ok && ks.valid; ++i) {
     ok = load_K(ks);
     tile_next(ks, p, &csr_bad);
+    if (ok) ok = publish();
   }
   while (ok && vs.valid) {
     ok = load_tile(tv, vs.it.bh * p.T + key_block(vs) * kBlk);
@@ -424,8 +501,9 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
     if (ks.valid) {
       ok = load_K(ks);
       tile_next(ks, p, &csr_bad);
+      if (ok) ok = publish();
     }
-    tile_next(vs, p, nullptr);
+    ring_tile_next(vs, sh, p);
   }
   if (csr_bad && leader) raise_error(p, BSATTN_E_CSR);
   // No TMA write may still be landing in shared memory when the CTA exits.  On a normal run every
@@ -463,7 +541,7 @@ __device__ void mma_s_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem)
   // Test hook for the timeout path: a wait that can only end by running out of time.
   if (p.test_unsignalled_wait && !wait_ctl(ptx::smem_u32(&sh.unsignalled), 0, sh, p)) return;
   TileIter x;
-  tile_begin(x, p, nullptr);
+  ring_tile_begin(x, sh, p);
   while (x.valid) {
     const int qb = x.ii & 1;
     const int sb = x.t & 1;
@@ -489,7 +567,7 @@ __device__ void mma_s_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem)
     ptx::tc_commit(kv_empty0 + stage * 8);
     ptx::tc_commit(ptx::smem_u32(&sh.s_full[sb]));
     if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.q_empty[qb]));
-    tile_next(x, p, nullptr);
+    ring_tile_next(x, sh, p);
   }
 }
 
@@ -498,9 +576,9 @@ __device__ void mma_pv_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem
   const uint32_t kv_full0 = ptx::smem_u32(&sh.kv_full[0]);
   const uint32_t kv_empty0 = ptx::smem_u32(&sh.kv_empty[0]);
   TileIter x, nx;  // nx = the tile after x (tells whether x is the CTA's last tile)
-  tile_begin(x, p, nullptr);
+  ring_tile_begin(x, sh, p);
   nx = x;
-  if (nx.valid) tile_next(nx, p, nullptr);
+  if (nx.valid) ring_tile_next(nx, sh, p);
   while (x.valid) {
     const int ob = x.ii & 1;
     const int sb = x.t & 1;
@@ -530,7 +608,7 @@ __device__ void mma_pv_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem
     ptx::tc_commit(ptx::smem_u32(&sh.pv_done[sb]));
     if (x.j == x.it.n_steps - 1) ptx::tc_commit(ptx::smem_u32(&sh.o_full[ob]));
     x = nx;
-    if (nx.valid) tile_next(nx, p, nullptr);
+    if (nx.valid) ring_tile_next(nx, sh, p);
   }
 }
 
@@ -548,11 +626,15 @@ __device__ void softmax_role(SharedStorage& sh, const FwdParams& p, int half, ui
   int tile = 0;
   int ii = 0;
 
-  ItemCursor cur;
-  cursor_begin(cur, p);
-  for (int g = cursor_next(cur, p); g >= 0; g = cursor_next(cur, p)) {
-    const Item it = load_item(p, g, nullptr);
-    if (it.n_steps == 0) continue;  // the epilogue warpgroup writes inactive items
+  // Active items from the item ring (the epilogue warpgroup writes the inactive ones).
+  for (;; ++ii) {
+    const int slot = ii & (kItemRing - 1);
+    if (!wait_warp(ptx::smem_u32(&sh.item_full[slot]), static_cast<uint32_t>(ii / kItemRing) & 1u,
+                   sh, p))
+      return;
+    const Item it = sh.items[slot];
+    ptx::mbar_arrive(ptx::smem_u32(&sh.item_empty[slot]));
+    if (it.n_steps == 0) break;
     const int ob = ii & 1;
     const bool row_valid = it.qb * kBlk + t < it.seq_len;
     float m_run = -1e30f;  // v4 :74
@@ -678,7 +760,6 @@ __device__ void softmax_role(SharedStorage& sh, const FwdParams& p, int half, ui
     if (half == 0) sh.stats[ob][0][t] = m_run;
     sh.stats[ob][1 + half][t] = l_run;
     ptx::mbar_arrive(ptx::smem_u32(&sh.stats_rdy[ob]));
-    ++ii;
   }
 }
 
@@ -820,6 +901,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     ptx::mbar_init(ptx::smem_u32(&sh.pv_done[1]), 1);
     for (int b = 0; b < 2; ++b)
       for (int q = 0; q < 4; ++q) ptx::mbar_init(ptx::smem_u32(&sh.xchg[b][q]), 64);
+    for (int i = 0; i < kItemRing; ++i) {
+      ptx::mbar_init(ptx::smem_u32(&sh.item_full[i]), 1);
+      ptx::mbar_init(ptx::smem_u32(&sh.item_empty[i]), kItemReaders);
+    }
     ptx::mbar_init(ptx::smem_u32(&sh.drain), 2);  // one commit per MMA-issuing thread
     ptx::mbar_init(ptx::smem_u32(&sh.unsignalled), 1);
     sh.abort_flag = 0;
