@@ -36,6 +36,10 @@
 //   * MMA issue is split: one warp issues every S(t) = Q K(t)^T (after PV(t-2) finished with the
 //     S buffer), another every PV(t); the producer loads tiles in the order K0, K1, V0, K2, V1, ...
 //     that the two warps consume them.
+//   * Item descriptors (head, query block, seq_len, tile count, CSR row start) are loaded from
+//     global memory once, by the producer, and handed to the softmax warpgroups and the MMA
+//     issuers through an 8-slot ring in shared memory: no critical role waits on a dependent chain
+//     of global loads (work list, then row_ptr and seq_lens) at an item boundary.
 //   * Lazy rescale: the running row max m is raised only when a block's max exceeds it by more
 //     than kRescaleLog2 (P stays <= 2^8 in fp16); the final o = O/l and lse are exact.
 //   * Every mbarrier wait is bounded (globaltimer); on expiry the CTA raises an abort flag, all
@@ -472,6 +476,7 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
     return x.j < x.it.n_steps - 1 ? offdiag_block(p, x.it, x.j, nullptr) : x.it.qb;
   };
   // ks publishes each new active item (and the end marker) to the item ring.
+  tile_begin(ks, p, &csr_bad);
   int published = 0;
   auto publish = [&]() -> bool {
     if (ks.valid) {
@@ -486,7 +491,6 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
     end.n_steps = 0;
     return ring_write(sh, p, ks.ii, end);
   };
-  tile_begin(ks, p, &csr_bad);
   ok = publish();
   if (ok) ring_tile_begin(vs, sh, p);
   else vs.valid = false;
