@@ -11,6 +11,12 @@ Multi-GPU: one process per GPU (torchrun); every rank runs the same per-GPU work
 (weak scaling).  The optional NCCL gather of o to rank 0 is timed separately (``gather_ms``).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload families|mix]
+
+``--workload mix`` measures the head-sharded scaling configuration instead: one B=4, H=32,
+T=32768 problem whose heads cycle through window16 / prefix8+window8 / retrieval(2+16), its 128
+(batch, head) pairs split contiguously across the N ranks (strong scaling: the total work is
+fixed), o gathered to rank 0 over NCCL and timed separately.
 
 ``--impl reference`` times the reference's CPU path (the dense-masked fp32 restatement in
 oracle/, the reference having no CPU implementation of its own) on the host cores, rank 0 only.
@@ -235,6 +241,184 @@ def _pattern_flops(fam):
     return _FLOPS_CACHE[fam]
 
 
+MIX_B, MIX_H, MIX_T = 4, 32, 32768
+MIX_METRIC = ("ms/call + live-block TFLOP/s, head-sharded scaling mix (B=4,H=32,T=32768,D=128) "
+              "vs B200 fp16 TC peak")
+
+
+def init_distributed(world, device):
+    """NCCL process group for world > 1.  NCCL announces itself on stdout when the communicator is
+    created; that goes to stderr so stdout carries only the JSON line."""
+    import datetime
+    import torch.distributed as dist
+    if world <= 1:
+        return
+    sys.stdout.flush()
+    saved_fd = os.dup(1)
+    os.dup2(2, 1)
+    try:
+        dist.init_process_group("nccl", device_id=device, timeout=datetime.timedelta(seconds=120))
+        dist.barrier()
+        torch.cuda.synchronize()
+    finally:
+        sys.stdout.flush()
+        os.dup2(saved_fd, 1)
+        os.close(saved_fd)
+
+
+def run_mix(args, rank, world, local_rank):
+    """Strong scaling over the scaling-mix problem: each rank runs the kernel on its contiguous
+    share of the 128 (batch, head) pairs; value = live FLOPs of the whole problem / the max over
+    ranks of the device time of K calls."""
+    import torch.distributed as dist
+    import usagi_b200 as ub
+    from usagi_b200 import patterns as P
+    from usagi_b200 import shard
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    init_distributed(world, device)
+    ub.setup(device=str(device))
+    peaks = load_peaks()
+    pat = P.mixed_pattern(MIX_B, MIX_H, MIX_T)  # host, identical on every rank (seed 1)
+    total_heads = MIX_B * MIX_H
+    if total_heads % world:
+        raise SystemExit(f"--workload mix needs N dividing {total_heads}")
+    g = torch.Generator(device=device).manual_seed(11)
+    shape = (MIX_B, MIX_H, MIX_T, D)
+    full = [torch.randn(shape, generator=g, device=device, dtype=torch.float32).half()
+            for _ in range(3)]  # the same problem on every rank; each keeps its heads
+    q, k, v, rp, ci, _, (h0, h1) = shard.shard_problem(*full, pat.row_ptr, pat.col_idx, None,
+                                                       world, rank)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    del full
+    n = h1 - h0
+    rp_d, ci_d = rp.to(device), ci.to(device)
+    plan = ub.make_plan(rp, ci, n, 1, MIX_T, device=device)
+    o = torch.empty_like(q)
+    lse = torch.empty((n, 1, MIX_T), device=device, dtype=torch.float32)
+    rp_bh = pat.row_ptr.reshape(total_heads, -1).to(torch.int64)
+    live_rank = int((rp_bh[h0:h1, -1] - rp_bh[h0:h1, 0]).sum())
+    flops_total = pat.live_blocks() * 4 * 128 ** 3
+    flops_rank = live_rank * 4 * 128 ** 3
+
+    def call():
+        ub.block_sparse_attn_fwd(q, k, v, rp_d, ci_d, None, out=o, lse_out=lse, plan=plan)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    ub.check_errors(device)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+          for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local_rank) as clk:
+        for a, b in ev:
+            a.record()
+            call()
+            b.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    ub.check_errors(device)
+    total_ms = sum(a.elapsed_time(b) for a, b in ev)
+    t = torch.tensor([total_ms], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item()) / args.steps
+    rank_ms = total_ms / args.steps
+
+    # End to end on this rank's share: its q, k, v, CSR rows and work list up from pinned host
+    # memory, the call, o and lse back, every step.
+    host_in = [x.cpu().pin_memory() for x in (q, k, v, rp_d, ci_d, plan.tensor)]
+    dev_in = [torch.empty_like(x) for x in (q, k, v, rp_d, ci_d, plan.tensor)]
+    host_out = (torch.empty(o.shape, dtype=o.dtype).pin_memory(),
+                torch.empty(lse.shape, dtype=lse.dtype).pin_memory())
+    h2d = sum(x.numel() * x.element_size() for x in host_in)
+    d2h = sum(x.numel() * x.element_size() for x in host_out)
+
+    def e2e_step():
+        for d_, h_ in zip(dev_in, host_in):
+            d_.copy_(h_, non_blocking=True)
+        pl = ub.Plan(dev_in[5], plan.grid, plan.B, plan.H, plan.T)
+        ub.block_sparse_attn_fwd(dev_in[0], dev_in[1], dev_in[2], dev_in[3], dev_in[4], None,
+                                 out=o, lse_out=lse, plan=pl)
+        host_out[0].copy_(o, non_blocking=True)
+        host_out[1].copy_(lse, non_blocking=True)
+
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n_e2e = max(3, min(args.steps, 5))
+    e0.record()
+    for _ in range(n_e2e):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / n_e2e], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_ms = float(te.item())
+    assert torch.equal(host_out[0].to(device), o)
+
+    gather_ms = None
+    if world > 1 and not args.no_gather:
+        gather_ms = shard.timed_gather_to_root(o, world, rank, device)
+    clocks = clk.summary()
+    line = {
+        "metric": MIX_METRIC,
+        "value": flops_total / (ms * 1e-3) / 1e12,
+        "unit": "TFLOP/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": ms,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": "f16",
+        "data": "synthetic (seeded N(0,1) fp16; mixed CSR pattern, seed 1)",
+        "config": {
+            "workload": "scaling mix B=4,H=32,T=32768,D=128: heads cycle window16 / "
+                        "prefix8+window8 / retrieval(2+16); one step = one call on each rank's "
+                        "share",
+            "global_batch": MIX_B, "heads": MIX_H, "seq_len": MIX_T, "head_dim": D,
+            "live_blocks": pat.live_blocks(),
+            "parallelism": f"heads split contiguously x{world} ({n} (batch, head) pairs per rank), "
+                           "no collective on the data path",
+            "l2": "inputs (3 GiB at N=1) larger than L2, no flush",
+            "schedule": "balanced work list (bsattn_plan) per rank",
+        },
+        "gpu_launches": args.steps,
+        "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+                "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "path": "usagi_b200.block_sparse_attn_fwd from pinned host buffers, per rank"},
+        "clocks": clocks,
+        "roofline": {
+            "bound": "tensor", "kernel": "bsattn_fwd_kernel",
+            "achieved": flops_rank / (rank_ms * 1e-3) / 1e12, "peak": peaks["bf16_tflops"],
+            "peak_source": peaks["source"] + " bf16 dense burst (fp16 runs at the same rate)",
+            "unit": "TFLOP/s",
+            "frac": flops_rank / (rank_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+            "algorithmic": "live tiles x 4*128^3 FLOP of rank 0's share per launch",
+            "traffic": None,
+        },
+    }
+    if gather_ms is not None:
+        line["gather_ms"] = gather_ms
+        line["kernel_plus_gather_ms"] = ms + gather_ms
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 # Window families whose rows also have the analytic form of bsattn_fwd_window: (window, global).
 ANALYTIC = {"window8": (8, 0), "prefix4+window4": (4, 4)}
 
@@ -378,6 +562,9 @@ def main():
                     help="round-robin item order instead of the balanced work list")
     ap.add_argument("--family", choices=FAMILIES, default=None,
                     help="run one family only (profiling); the JSON line then covers that family")
+    ap.add_argument("--workload", choices=["families", "mix"], default="families",
+                    help="families: the headline 3-family workload (weak scaling); mix: the "
+                         "head-sharded scaling configuration (strong scaling)")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed region only: no e2e, cpu_baseline or gather (profiling)")
     args = ap.parse_args()
@@ -394,8 +581,9 @@ def main():
 
     if args.impl == "reference":
         return run_reference(args, rank, world)
+    if args.workload == "mix":
+        return run_mix(args, rank, world, local_rank)
 
-    import datetime
     import torch.distributed as dist
     import usagi_b200 as ub
     from usagi_b200 import shard
@@ -404,21 +592,7 @@ def main():
     device = torch.device("cuda", local_rank)
     if os.environ.get("NCCL_DEBUG", "").upper() == "VERSION":
         os.environ["NCCL_DEBUG"] = "WARN"  # keep stdout to the single JSON line
-    if world > 1:
-        # NCCL announces itself on stdout when the communicator is created; send that to stderr so
-        # stdout carries only the JSON line.
-        sys.stdout.flush()
-        saved_fd = os.dup(1)
-        os.dup2(2, 1)
-        try:
-            dist.init_process_group("nccl", device_id=device,
-                                    timeout=datetime.timedelta(seconds=120))
-            dist.barrier()
-            torch.cuda.synchronize()
-        finally:
-            sys.stdout.flush()
-            os.dup2(saved_fd, 1)
-            os.close(saved_fd)
+    init_distributed(world, device)
     ub.setup(device=str(device))
 
     peaks = load_peaks()
