@@ -73,19 +73,9 @@ __device__ __forceinline__ void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
 }
 
-// 2-D tiled bulk tensor load global -> shared, completion signalled on `bar` (complete_tx).
-// x is the innermost (contiguous) coordinate in elements; callers keep x * 2 bytes a multiple
-// of 16 (x is 0 or 64 here).
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t bar, int x,
-                                            int y, uint64_t cache_policy) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
-      "l"(tmap), "r"(x), "r"(y), "r"(bar), "l"(cache_policy)
-      : "memory");
-}
-
-// 3-D tiled bulk tensor load (one instruction for a whole 128x128 tile, see make_tile_map).
+// 3-D tiled bulk tensor load global -> shared, completion signalled on `bar` (complete_tx); one
+// instruction moves a whole 128x128 tile (see make_tile_map).  x is the innermost (contiguous)
+// coordinate in elements; callers keep x * 2 bytes a multiple of 16 (x is 0 here).
 __device__ __forceinline__ void tma_load_3d(uint32_t dst, const void* tmap, uint32_t bar, int x,
                                             int y, int z, uint64_t cache_policy) {
   asm volatile(
