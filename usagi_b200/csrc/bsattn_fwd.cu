@@ -11,8 +11,9 @@
 //   Query blocks starting at or past seq_len write o = 0, lse = -inf (v4 :63-68).
 //
 // How (B200-native design, not a translation of the Triton program):
-//   * Persistent CTAs, one per SM.  Work items (bh, qb) are dealt round-robin, in groups of heads
-//     whose K/V fit in L2 and, within a group, in order of decreasing qb (longest rows first).  Each CTA streams its items' 128x128 tiles
+//   * Persistent CTAs, one per SM.  Work items (bh, qb) are ordered in groups of heads whose K/V
+//     fit in L2 and, within a group, by decreasing qb (longest rows first); CTAs take them from a
+//     balanced work list (bsattn_plan) or round robin.  Each CTA streams its items' 128x128 tiles
 //     through one continuous pipeline: tile t of the CTA uses S buffer t%2, item i uses Q and O
 //     buffers i%2, so the next tile's QK^T and the next item's MMAs overlap the current softmax
 //     and the previous item's epilogue.
