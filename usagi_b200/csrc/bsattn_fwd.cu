@@ -304,7 +304,9 @@ __device__ __forceinline__ void epi_sync() { asm volatile("bar.sync 1, 128;" :::
 // Same barrier with an OR over the warpgroup: every thread gets true when any thread passed true.
 __device__ __forceinline__ bool epi_any(bool v) {
   uint32_t r;
-  asm volatile("{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\tbar.red.or.pred b, 1, 128, a;\n\tselp.u32 %0, 1, 0, b;\n\t}"
+  asm volatile(
+      "{\n\t.reg .pred a, b;\n\tsetp.ne.u32 a, %1, 0;\n\tbar.red.or.pred b, 1, 128, a;"
+      "\n\tselp.u32 %0, 1, 0, b;\n\t}"
                : "=r"(r) : "r"(v ? 1u : 0u) : "memory");
   return r != 0;
 }
@@ -529,9 +531,9 @@ __device__ void producer_role(SharedStorage& sh, const CUtensorMap* tq, const CU
 // S(t) overwrites the S buffer that held P(t-2), hence the wait on pv_done before it.  Each role
 // runs on lane 0 and commits its own MMAs.  Ring positions follow the producer's load order
 // K0, K1, V0, K2, V1, K3, ...: K(t) sits at position t for t < 2 and 2t-1 after; V(t) at 2t+2,
-// except for the CTA's last tile, whose V follows V(t-1) directly (no K(t+1) exists) at 2t+1.  Descriptors are
-// advanced by adding (byte offset >> 4) to the start-address field, which never carries out of
-// its 14 bits inside 227 KB of shared memory.
+// except for the CTA's last tile, whose V follows V(t-1) directly (no K(t+1) exists) at 2t+1.
+// Descriptors are advanced by adding (byte offset >> 4) to the start-address field, which never
+// carries out of its 14 bits inside 227 KB of shared memory.
 // ------------------------------------------------------------------------------------------
 __device__ __forceinline__ void ring_slot(int pos, int& stage, uint32_t& phase) {
   stage = pos % kStages;
@@ -593,7 +595,8 @@ __device__ void mma_pv_role(SharedStorage& sh, const FwdParams& p, uint32_t tmem
     ring_slot(nx.valid ? 2 * x.t + 2 : 2 * x.t + 1, stage, phase);
     if (!wait_ctl(kv_full0 + stage * 8, phase, sh, p)) return;
     if (x.j == 0 && x.ii >= 2 &&  // O[ob] read out by the epilogue of item ii-2
-        !wait_ctl(ptx::smem_u32(&sh.o_free[ob]), ((static_cast<uint32_t>(x.ii) >> 1) + 1u) & 1u, sh, p))
+        !wait_ctl(ptx::smem_u32(&sh.o_free[ob]), ((static_cast<uint32_t>(x.ii) >> 1) + 1u) & 1u, sh,
+                  p))
       return;
     if (!wait_ctl(ptx::smem_u32(&sh.p_rdy[sb][0]), tph, sh, p)) return;
     if (!wait_ctl(ptx::smem_u32(&sh.p_rdy[sb][1]), tph, sh, p)) return;
