@@ -28,18 +28,23 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q):
+def _worker(rank, world, port, q, kind):
     import torch.distributed as dist
     from oracle.bsattn_oracle import attn_blockwise
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
-        B, H, T = 2, 3, 512
+        if kind == "retrieval":
+            B, H, T = 2, 3, 512
+            pat = P.retrieval_pattern(B, H, T, 4, seed=1)
+            sl = torch.tensor([512, 300], dtype=torch.int32)
+        else:  # the scaling mix's head-dependent families; 4 heads over 3 ranks are uneven
+            B, H, T = 1, 4, 2048
+            pat = P.mixed_pattern(B, H, T)
+            sl = None
         g = torch.Generator().manual_seed(0)
         qq, kk, vv = [torch.randn(B, H, T, 128, generator=g).half() for _ in range(3)]
-        pat = P.retrieval_pattern(B, H, T, 4, seed=1)
-        sl = torch.tensor([512, 300], dtype=torch.int32)
         sq, sk, sv, srp, sci, ssl, (s0, s1) = shard.shard_problem(qq, kk, vv, pat.row_ptr,
                                                                   pat.col_idx, sl, world, rank)
         o_shard, _ = attn_blockwise(sq, sk, sv, srp, sci, ssl)
@@ -51,12 +56,12 @@ def _worker(rank, world, port, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2])
-def test_sharded_oracle_gathers_to_full_result(world):
+@pytest.mark.parametrize("world,kind", [(2, "retrieval"), (3, "mixed")])
+def test_sharded_oracle_gathers_to_full_result(world, kind):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q, kind)) for r in range(world)]
     for p in procs:
         p.start()
     for p in procs:
