@@ -126,3 +126,79 @@ def test_window_plan_argument_errors():
     assert lib.bsattn_plan_window(None, 1, 1, 256, 4, 0, 2, None, 256) == _lib.E_NULL
     assert lib.bsattn_plan_window(None, 1, 1, 256, 4, 0, 2, buf.data_ptr(), 8) == _lib.E_WORKSPACE
     assert lib.bsattn_plan_window(None, 1, 1, 256, 4, 0, 2, buf.data_ptr(), 256) == _lib.OK
+
+
+def _sizes_rows(rp_bh, B, H, T, max_nnz, seq_lens):
+    """Tile counts in the kernel's item order for explicit per-head row offsets, including the
+    rule that a row whose range does not fit the max_nnz columns counts as its diagonal alone."""
+    nqb, BH = T // 128, B * H
+    gh = max(1, min(BH, (32 << 20) // (512 * T)))
+    per = gh * nqb
+    out = []
+    for g in range(BH * nqb):
+        grp, r = divmod(g, per)
+        ghh = min(gh, BH - grp * gh)
+        band = r // ghh
+        bh, qb = grp * gh + (r - band * ghh), nqb - 1 - band
+        sl = T if seq_lens is None else min(int(seq_lens[bh // H]), T)
+        if qb * 128 >= sl:
+            out.append(0)
+            continue
+        rs, re = int(rp_bh[bh][qb]), int(rp_bh[bh][qb + 1])
+        n_off = max(re - rs - 1, 0)
+        if n_off > 0 and (rs < 0 or rs + n_off > max_nnz):
+            n_off = 0
+        out.append(n_off + 1)
+    return out
+
+
+def test_plan_properties_on_random_rows():
+    """Any row lengths, seq_lens and grid: the list is an exact permutation of the items, every
+    CTA's items are sorted by tile count (ties in item order), and the snake deal keeps the CTA
+    loads within one largest item of each other."""
+    hyp = pytest.importorskip("hypothesis")
+    st = hyp.strategies
+
+    @hyp.settings(max_examples=80, deadline=None, derandomize=True)
+    @hyp.given(st.data())
+    def check(data):
+        B = data.draw(st.integers(1, 3))
+        H = data.draw(st.integers(1, 4))
+        nqb = data.draw(st.integers(1, 12))
+        T, BH = 128 * nqb, B * H
+        lens = data.draw(st.lists(st.integers(0, 9), min_size=BH * nqb, max_size=BH * nqb))
+        rp_bh = []
+        for bh in range(BH):
+            offs = [0]
+            for i in range(nqb):
+                offs.append(offs[-1] + lens[bh * nqb + i])
+            rp_bh.append(offs)
+        max_nnz = data.draw(st.integers(0, max(o[-1] for o in rp_bh) + 2))
+        seq_lens = None
+        if data.draw(st.booleans()):
+            seq_lens = torch.tensor(data.draw(st.lists(st.integers(0, T + 64), min_size=B,
+                                                       max_size=B)), dtype=torch.int32)
+        items = BH * nqb
+        grid = data.draw(st.integers(1, items))
+        lib = _lib.load()
+        rp = torch.tensor(rp_bh, dtype=torch.int32).contiguous()
+        nb = ctypes.c_size_t(0)
+        assert lib.bsattn_plan_bytes(B, H, T, grid, ctypes.byref(nb)) == 0
+        buf = torch.empty(nb.value // 4, dtype=torch.int32)
+        rc = lib.bsattn_plan(rp.data_ptr(), nqb + 1,
+                             seq_lens.data_ptr() if seq_lens is not None else None, B, H, T,
+                             max_nnz, grid, buf.data_ptr(), nb.value)
+        assert rc == 0, _lib.strerror(rc)
+        assert buf[:4].tolist() == [MAGIC, grid, items, 0]
+        off = buf[4:4 + grid + 1].tolist()
+        lst = buf[4 + grid + 1:].tolist()
+        assert off[0] == 0 and off[-1] == items and all(a <= b for a, b in zip(off, off[1:]))
+        assert sorted(lst) == list(range(items))
+        size = _sizes_rows(rp_bh, B, H, T, max_nnz, seq_lens)
+        loads = [sum(size[g] for g in lst[off[c]:off[c + 1]]) for c in range(grid)]
+        assert max(loads) - min(loads) <= max(size)
+        for c in range(grid):
+            keys = [(-size[g], g) for g in lst[off[c]:off[c + 1]]]
+            assert keys == sorted(keys)
+
+    check()
