@@ -134,7 +134,9 @@ BSATTN_API int bsattn_plan_window(const int32_t* seq_lens, int B, int H, int T, 
  *   - Every call on a device shares the scratch.  Each call clears its error word on `stream`
  *     before the kernel; calls that overlap on the GPU (different streams) race on it.
  *   - status (optional, device or pinned host int*): receives 0, BSATTN_E_CSR or
- *     BSATTN_E_TIMEOUT for this call, written on `stream` after the kernel. */
+ *     BSATTN_E_TIMEOUT for this call, written on `stream` after the kernel.  When the call
+ *     itself returns non-zero (an argument or launch error), nothing was enqueued after the
+ *     failure point and *status is left untouched. */
 BSATTN_API int bsattn_fwd_noalloc(const void* q, const void* k, const void* v, void* o, float* lse,
                                   const int32_t* row_ptr, const int32_t* col_idx,
                                   const int32_t* seq_lens, int B, int H, int T, int D,

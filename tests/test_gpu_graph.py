@@ -92,3 +92,35 @@ def test_two_streams_overlap():
             with torch.cuda.stream(s):
                 ub.check_errors(DEV)
             assert torch.equal(outs[j][0], eager[j][0]) and torch.equal(outs[j][1], eager[j][1])
+
+
+def test_first_call_on_a_stream_inside_capture_is_refused():
+    """The first call on a stream creates and zeroes its error word; inside capture that fill
+    would only be recorded, so the call must refuse with a clear error instead."""
+    from usagi_b200 import api
+    B, H, T = 1, 1, 256
+    pat = P.window_pattern(B, H, T, 2)
+    rp, ci = pat.row_ptr.to(DEV), pat.col_idx.to(DEV)
+    q, k, v = [_randn((B, H, T, 128), 90 + i) for i in range(3)]
+    o = torch.empty_like(q)
+    lse = torch.empty((B, H, T), device=DEV)
+    fresh = torch.cuda.Stream(DEV)
+    fresh.wait_stream(torch.cuda.current_stream(DEV))
+    api._workspaces.pop((DEV.index, fresh.cuda_stream), None)  # as if never used
+    graph = torch.cuda.CUDAGraph()
+    with pytest.raises(RuntimeError, match="outside graph capture"):
+        with torch.cuda.graph(graph, stream=fresh):
+            ub.block_sparse_attn_fwd(q, k, v, rp, ci, None, out=o, lse_out=lse)
+    del graph
+    # after an eager warm-up on the stream, the same call captures and replays
+    with torch.cuda.stream(fresh):
+        ub.block_sparse_attn_fwd(q, k, v, rp, ci, None, out=o, lse_out=lse)
+    fresh.synchronize()
+    ref = o.clone()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph, stream=fresh):
+        ub.block_sparse_attn_fwd(q, k, v, rp, ci, None, out=o, lse_out=lse)
+    o.zero_()
+    graph.replay()
+    torch.cuda.synchronize()
+    assert torch.equal(o, ref)

@@ -104,3 +104,12 @@ def test_device_builder_validation():
     assert lib.bsattn_build_csr(_lib.CSR_WINDOW, 8, 0, 4, 0, 1, 1, None, 16, 64, None) == _lib.E_NULL
     assert lib.bsattn_build_csr(_lib.CSR_WINDOW, 8, 0, 4, 0, 1, 1, 16, 16, 3, None) == _lib.E_SHAPE
     assert lib.bsattn_build_csr(_lib.CSR_WINDOW, 8, 0, 4, 0, 1, 0, 16, 16, 64, None) == _lib.E_SHAPE
+    # prefix + window past INT_MAX (it would wrap the row arithmetic) is rejected up front
+    big = 2 ** 31 - 2
+    assert _nnz(_lib.CSR_PREFIX_WINDOW, 8, prefix=2, window=big)[0] == _lib.E_SHAPE
+    assert _nnz(_lib.CSR_PREFIX_WINDOW, 8, prefix=big, window=2)[0] == _lib.E_SHAPE
+    assert _nnz(_lib.CSR_WINDOW, 8, window=2 ** 24 + 1)[0] == _lib.E_SHAPE
+    assert lib.bsattn_build_csr(_lib.CSR_PREFIX_WINDOW, 8, 2, big, 0, 1, 1, 16, 16, 64,
+                                None) == _lib.E_SHAPE
+    # the largest accepted window still gives the closed-form count (every row is 0 .. i)
+    assert _nnz(_lib.CSR_PREFIX_WINDOW, 8, prefix=2 ** 24, window=2 ** 24) == (0, 36)

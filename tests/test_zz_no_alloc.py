@@ -1,7 +1,9 @@
 """GPU test of bsattn_fwd_noalloc, the entry point for callers that cannot allocate device memory
-(for example code running inside a memory arena it does not own): it must give the same output
-as bsattn_fwd, which takes a caller-allocated workspace, and it must work on consecutive calls,
-since every call on a GPU reuses the same fixed scratch array compiled into the library.
+(for example code running inside a memory arena it does not own): it runs the same kernel with
+the same grid as bsattn_fwd, which takes a caller-allocated workspace, so its output must equal
+that entry point's bit for bit, and it must do so on consecutive calls, since every call on a GPU
+reuses the same fixed scratch array compiled into the library.  One head is also checked against
+the fp32 oracle under the parity tolerance of the other GPU tests.
 
 This file is named to be collected last, so that a run stopping at the first failure has already
 run every other test.  It does not depend on state left by other tests.
@@ -14,11 +16,13 @@ import torch
 import usagi_b200 as ub
 from usagi_b200 import _lib, api
 from usagi_b200 import patterns as P
+from oracle.bsattn_oracle import attn_blockwise
 
 pytestmark = pytest.mark.gpu
 
 DEV = torch.device("cuda", 0)
-MAX_TOL, MEAN_TOL = 1e-2, 1e-3  # the parity tolerance the other GPU tests use
+MAX_TOL, MEAN_TOL = 1e-2, 1e-3  # the parity contract the other GPU tests use
+REG_MAX, REG_MEAN = 4e-3, 2e-4  # their regression bound against the fp32 oracle
 
 
 def _noalloc(q, k, v, row_ptr, col_idx, seq_lens, status):
@@ -59,11 +63,22 @@ def test_noalloc_matches_workspace_entry_point_on_consecutive_calls():
         assert rc == 0, _lib.strerror(rc)
         torch.cuda.synchronize()
         assert int(status.item()) == 0, f"call {call}: device status {int(status.item())}"
-        d = (o.float() - ref_o.float()).abs()
-        assert d.max().item() <= MAX_TOL and d.mean().item() <= MEAN_TOL, (call, d.max().item())
-        fin = torch.isfinite(ref_lse)
-        assert torch.equal(fin, torch.isfinite(lse))
-        assert (lse[fin] - ref_lse[fin]).abs().max().item() <= 2e-4
+        # same kernel, same grid, no work list: identical bits, not merely close values
+        assert torch.equal(o, ref_o), (call, (o.float() - ref_o.float()).abs().max().item())
+        assert torch.equal(lse, ref_lse), call
+    # one head (b=1: seq_len 1500 < T) against the fp32 oracle
+    H = q.shape[1]
+    bh = H + 2
+    sub = lambda t: t.reshape(-1, *t.shape[2:])[bh:bh + 1].unsqueeze(0).cpu()  # noqa: E731
+    rps = rp.reshape(-1, rp.shape[-1])[bh:bh + 1].reshape(1, 1, -1).cpu()
+    cis = ci.reshape(-1, ci.shape[-1])[bh:bh + 1].reshape(1, 1, -1).cpu()
+    ro, rl = attn_blockwise(sub(q), sub(k), sub(v), rps, cis, sl[1:2].cpu())
+    d = (sub(o).float() - ro).abs()
+    assert d.max().item() <= REG_MAX and d.mean().item() <= REG_MEAN, d.max().item()
+    assert d.max().item() <= MAX_TOL and d.mean().item() <= MEAN_TOL
+    fin = torch.isfinite(rl)
+    assert torch.equal(fin, torch.isfinite(sub(lse)))
+    assert (sub(lse)[fin] - rl[fin]).abs().max().item() <= 2e-4
 
 
 def test_noalloc_status_is_per_call():

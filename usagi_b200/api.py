@@ -62,10 +62,19 @@ _workspaces: dict = {}
 
 
 def _workspace(device: torch.device, stream: int) -> torch.Tensor:
+    """The error-word workspace of one (device, CUDA stream handle), created and zeroed on first
+    use.  The zero fill must run eagerly: inside stream capture it would only be recorded (and
+    run at replay), leaving the word uninitialised for eager calls, so a first use during capture
+    is refused -- call once on the stream before capturing it, as a warm-up."""
     key = (device.index, stream)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError(
+                    "usagi_b200: the first call on a CUDA stream must run outside graph capture "
+                    "(it creates and zeroes the stream's error word); make one eager call on this "
+                    "stream before capturing it")
             n = _lib.load().bsattn_workspace_bytes()
             ws = torch.zeros((n + 3) // 4, dtype=torch.int32, device=device)
             _workspaces[key] = ws
@@ -320,7 +329,12 @@ def block_sparse_attn_fwd_window(q: torch.Tensor, k: torch.Tensor, v: torch.Tens
 
 
 def check_errors(device=None) -> None:
-    """Synchronise and raise if a kernel on this device/stream reported a CSR or timeout error."""
+    """Synchronise and raise if a kernel on this device/stream reported a CSR or timeout error.
+
+    The error word belongs to the CUDA stream handle, not to a ``torch.cuda.Stream`` object:
+    torch hands out pooled stream handles again to later Stream objects, so an error that no
+    check collected is reported by the next check on the same handle.  Checking clears it; call
+    this before handing a pooled stream to unrelated work if errors must not carry over."""
     lib = _lib.load()
     dev = torch.device(device) if device is not None else torch.device("cuda",
                                                                          torch.cuda.current_device())

@@ -9,6 +9,7 @@ Usage: ``python -m usagi_b200.build [--force]``
 """
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -20,6 +21,8 @@ CSRC = PKG_DIR / "csrc"
 INCLUDE = PKG_DIR.parent / "include"
 LIB_NAME = "libbsattn.so"
 LIB_PATH = PKG_DIR / LIB_NAME
+# Hash of the sources, headers and flags the in-tree library was built from (written next to it).
+STAMP_PATH = PKG_DIR / (LIB_NAME + ".sha256")
 
 SOURCES = ["bsattn_fwd.cu", "csr_build.cu"]
 HEADERS = ["sm100_ptx.cuh"]
@@ -49,11 +52,22 @@ def _inputs():
     return files
 
 
+def source_hash() -> str:
+    """sha256 over the compile flags and the bytes of every source and header of the library."""
+    h = hashlib.sha256()
+    h.update(" ".join(NVCC_FLAGS).encode())
+    for f in _inputs():
+        h.update(f.name.encode())
+        h.update(f.read_bytes())
+    return h.hexdigest()
+
+
 def needs_build() -> bool:
-    if not LIB_PATH.exists():
+    """True unless the in-tree library exists and its stamp names the current sources: a library
+    built from other sources (whatever its file time) is rebuilt."""
+    if not LIB_PATH.exists() or not STAMP_PATH.exists():
         return True
-    t = LIB_PATH.stat().st_mtime
-    return any(f.stat().st_mtime > t for f in _inputs())
+    return STAMP_PATH.read_text().strip() != source_hash()
 
 
 def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) -> Path:
@@ -72,7 +86,9 @@ def build(force: bool = False, verbose: bool = False, ptxas_info: bool = False) 
         raise RuntimeError(f"nvcc failed ({res.returncode}):\n{res.stdout}\n{res.stderr}")
     if verbose or ptxas_info:
         sys.stdout.write(res.stderr)
+    digest = source_hash()
     os.replace(tmp, LIB_PATH)
+    STAMP_PATH.write_text(digest + "\n")
     return LIB_PATH
 
 

@@ -19,6 +19,9 @@
 namespace bsattn_csr {
 
 constexpr int kMaxRandom = 64;
+// Largest prefix or window accepted (the same bound as the analytic rows of the attention entry
+// point): prefix + window then stays far below INT_MAX, so the row arithmetic cannot wrap.
+constexpr int kMaxWindow = 1 << 24;
 
 struct Spec {
   int kind, nqb, prefix, window, n_random;
@@ -59,7 +62,7 @@ __global__ void __launch_bounds__(256) build_kernel(Spec s, uint64_t seed, int n
   if (i == s.nqb - 1) rp[s.nqb] = static_cast<int32_t>(row_start(s, s.nqb));
 
   if (s.kind != BSATTN_CSR_RETRIEVAL) {
-    const int L = s.prefix + s.window;
+    const long long L = static_cast<long long>(s.prefix) + s.window;
     if (i < L) {
       for (int c = 0; c <= i; ++c) out[c] = c;
     } else {
@@ -101,7 +104,8 @@ static int validate(const Spec& s) {
   if (s.kind == BSATTN_CSR_RETRIEVAL) {
     if (s.n_random < 0 || s.n_random > kMaxRandom) return BSATTN_E_SHAPE;
   } else {
-    if (s.window < 1 || s.prefix < 0) return BSATTN_E_SHAPE;
+    if (s.window < 1 || s.prefix < 0 || s.window > kMaxWindow || s.prefix > kMaxWindow)
+      return BSATTN_E_SHAPE;
     if (s.kind == BSATTN_CSR_WINDOW && s.prefix != 0) return BSATTN_E_SHAPE;
   }
   if (row_start(s, s.nqb) >= (1ll << 31)) return BSATTN_E_SHAPE;
