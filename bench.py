@@ -54,8 +54,20 @@ def load_peaks():
         return dict(FALLBACK_PEAKS)
 
 
+def kernel_source_sha256() -> str:
+    """sha256 over the kernel's source files (the capture in profiles/ names the one it measured)."""
+    import hashlib
+    h = hashlib.sha256()
+    for name in ("bsattn_fwd.cu", "sm100_ptx.cuh"):
+        with open(os.path.join(ROOT, "usagi_b200", "csrc", name), "rb") as f:
+            h.update(f.read())
+    return h.hexdigest()
+
+
 def load_traffic():
-    """Per-launch DRAM bytes of the kernel from the committed ncu summary (or None)."""
+    """Per-launch DRAM bytes of the kernel from the committed ncu summary, or None.  The summary
+    carries the sha256 of the kernel source it was captured from; when the source has changed
+    since, the number no longer describes this kernel and is not reported."""
     path = os.path.join(ROOT, "profiles", "bsattn_fwd_traffic.txt")
     try:
         out = {}
@@ -64,9 +76,12 @@ def load_traffic():
                 if ":" in line and not line.startswith("#"):
                     k, v = line.split(":", 1)
                     out[k.strip()] = v.strip()
-        return out
     except Exception:
         return None
+    if out.get("kernel_source_sha256") != kernel_source_sha256():
+        return {"note": "stale: the committed DRAM capture was taken from another kernel source "
+                        "(sha256 mismatch), so no traffic is reported"}
+    return out
 
 
 class ClockSampler:
@@ -133,6 +148,45 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(self.samples), "source": "nvml"}
 
 
+def numa_info(gpu_index: int) -> dict:
+    """NUMA node of the GPU (sysfs, through its PCI bus id) and of the CPUs this process may run
+    on: where pinned host buffers land relative to the GPU's PCIe root."""
+    out = {"gpu_numa_node": None, "process_cpu_numa_nodes": None}
+    try:
+        import pynvml
+        pynvml.nvmlInit()
+        bus = pynvml.nvmlDeviceGetPciInfo(pynvml.nvmlDeviceGetHandleByIndex(gpu_index)).busId
+        bus = bus.decode() if isinstance(bus, bytes) else bus
+        dom, rest = bus.lower().split(":", 1)
+        path = f"/sys/bus/pci/devices/{dom[-4:]}:{rest}/numa_node"
+        with open(path) as f:
+            out["gpu_numa_node"] = int(f.read().strip())
+    except Exception:
+        pass
+    try:
+        cpus = os.sched_getaffinity(0)
+        nodes = set()
+        base = "/sys/devices/system/node"
+        for name in os.listdir(base):
+            if not name.startswith("node"):
+                continue
+            with open(os.path.join(base, name, "cpulist")) as f:
+                spec = f.read().strip()
+            ids = set()
+            for part in spec.split(","):
+                if "-" in part:
+                    a, b = part.split("-")
+                    ids.update(range(int(a), int(b) + 1))
+                elif part:
+                    ids.add(int(part))
+            if ids & cpus:
+                nodes.add(int(name[4:]))
+        out["process_cpu_numa_nodes"] = sorted(nodes)
+    except Exception:
+        pass
+    return out
+
+
 def make_inputs(device, rank, fam):
     from usagi_b200 import patterns as P
     g = torch.Generator(device=device).manual_seed(1000 * rank + FAMILIES.index(fam))
@@ -188,25 +242,57 @@ def cpu_reference_throughput(budget_s: float, threads: int):
                    f"{n_heads} whole heads (T=8192) of the 3 families ({per_fam}); "
                    f"{t_used:.1f}s; live-block FLOPs of the sampled heads / CPU time"),
         "ms_per_head": 1e3 * t_used / n_heads,
+        "heads": n_heads,
+        "seconds": t_used,
     }
 
 
+def cpu_config0(threads: int, reps: int = 5) -> dict:
+    """The reference's CPU-runnable configuration itself: B=1, H=2, T=1024, D=128, window of 4
+    blocks, q, k, v ~ N(0,1) fp32 from seed 0 (drawn in q, k, v order), through the same
+    dense-masked fp32 path; median of `reps` warm calls."""
+    from oracle.bsattn_oracle import attn_dense_masked
+    from usagi_b200 import patterns as P
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(0)
+    q, k, v = [torch.randn(1, 2, 1024, D, generator=g) for _ in range(3)]
+    pat = P.window_pattern(1, 2, 1024, 4, shared=False)
+    attn_dense_masked(q, k, v, pat.row_ptr, pat.col_idx)  # first call: allocation, threads
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        attn_dense_masked(q, k, v, pat.row_ptr, pat.col_idx)
+        ts.append(time.perf_counter() - t0)
+    ms = 1e3 * statistics.median(ts)
+    flops = pat.live_blocks() * 4 * 128 ** 3
+    return {"config": "B=1,H=2,T=1024,D=128, window 4, fp32, seed 0 (BASELINE config 0)",
+            "ms_per_call": ms, "value": flops / (ms * 1e-3) / 1e12, "unit": "TFLOP/s",
+            "live_blocks": pat.live_blocks(), "cores": threads, "reps": reps}
+
+
 def run_reference(args, rank, world):
+    """The reference arm: the reference's CPU path (its dense-masked fp32 restatement in
+    oracle/) on the host cores, rank 0 only.  A step is a bounded sample of the 3-family step:
+    whole heads, round robin over the families, for about --ref-budget seconds (at least one head
+    of each); its value is the sample's live-block FLOPs over its CPU time, and ms_per_step is
+    the measured wall time of that sample -- not a full 96-head step, which would take ~15 s."""
     if rank != 0:
         return 0
     threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
-    per_step = []
+    per_step, wall = [], []
     base = None
     # keep the whole --steps/--warmup run within a few minutes of CPU time
     budget = min(args.ref_budget, 150.0 / (args.warmup + args.steps))
     for s in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
         r = cpu_reference_throughput(budget_s=budget if s >= args.warmup else 0.0, threads=threads)
         if s >= args.warmup:
             per_step.append(r)
+            wall.append(time.perf_counter() - t0)
         base = r
     vals = [r["value"] for r in per_step]
     v = statistics.median(vals)
-    flops_step = sum(_pattern_flops(f) for f in FAMILIES)
+    heads = statistics.median(r["heads"] for r in per_step)
     line = {
         "impl": "reference",
         "metric": METRIC,
@@ -215,7 +301,11 @@ def run_reference(args, rank, world):
         "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup,
-        "ms_per_step": flops_step / (v * 1e12) * 1e3,
+        "ms_per_step": 1e3 * statistics.median(wall),
+        "ms_per_step_note": (f"measured wall time of one sampled step: about {heads:.0f} of the "
+                             f"{3 * B_PER_RANK * H} heads of a 3-family step (whole heads, round "
+                             "robin over the families); value is the sample's live-block FLOPs "
+                             "over its CPU time"),
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
@@ -224,7 +314,7 @@ def run_reference(args, rank, world):
         "config": {"workload": "3 families (window8, prefix4+window4, retrieval8) B=2,H=16,T=8192,D=128",
                    "parallelism": "host cores, rank 0 only"},
         "cpu_baseline": {"value": v, "unit": "TFLOP/s", "cores": base["cores"], "kind": "port",
-                         "sample": base["sample"]},
+                         "sample": base["sample"], "config0": cpu_config0(threads)},
         "e2e": {"value": v, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -266,24 +356,30 @@ def init_distributed(world, device):
         os.close(saved_fd)
 
 
-def run_mix(args, rank, world, local_rank):
-    """Strong scaling over the scaling-mix problem: each rank runs the kernel on its contiguous
-    share of the 128 (batch, head) pairs; value = live FLOPs of the whole problem / the max over
-    ranks of the device time of K calls."""
+MIX_CHUNKS = 4  # chunks per rank in the pipelined compute + gather of the scaling mix
+
+
+def measure_mix(args, rank, world, device, peaks):
+    """The head-sharded scaling configuration, strong scaling over the N ranks.
+
+    One B=4, H=32, T=32768 problem (heads cycle window16 / prefix8+window8 / retrieval 2+16); its
+    128 (batch, head) pairs are split contiguously across the ranks.  Two measurements:
+      * kernel: one call per rank on its whole share; ms = max over ranks of the device time;
+      * pipelined: each rank's share computed in MIX_CHUNKS chunks, each finished chunk sent to
+        rank 0 (NCCL point-to-point on a second stream) while the next one computes, received in
+        place into rank 0's [B*H, T, D] output; ms = max over ranks from the first launch until
+        rank 0 holds every head.  At N = 1 there is nothing to send: the chunked kernels alone.
+    Rank 0 then recomputes the first and last head of every rank's share on its own GPU and
+    checks that the gathered rows equal them bit for bit.  Returns (dict, extra) where extra
+    holds the tensors the standalone mix line needs for its end-to-end leg.
+    """
     import torch.distributed as dist
     import usagi_b200 as ub
     from usagi_b200 import patterns as P
     from usagi_b200 import shard
 
-    torch.cuda.set_device(local_rank)
-    device = torch.device("cuda", local_rank)
-    init_distributed(world, device)
-    ub.setup(device=str(device))
-    peaks = load_peaks()
     pat = P.mixed_pattern(MIX_B, MIX_H, MIX_T)  # host, identical on every rank (seed 1)
     total_heads = MIX_B * MIX_H
-    if total_heads % world:
-        raise SystemExit(f"--workload mix needs N dividing {total_heads}")
     g = torch.Generator(device=device).manual_seed(11)
     shape = (MIX_B, MIX_H, MIX_T, D)
     full = [torch.randn(shape, generator=g, device=device, dtype=torch.float32).half()
@@ -291,7 +387,9 @@ def run_mix(args, rank, world, local_rank):
     q, k, v, rp, ci, _, (h0, h1) = shard.shard_problem(*full, pat.row_ptr, pat.col_idx, None,
                                                        world, rank)
     q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    del full
+    if rank != 0:
+        del full
+        full = None
     n = h1 - h0
     rp_d, ci_d = rp.to(device), ci.to(device)
     plan = ub.make_plan(rp, ci, n, 1, MIX_T, device=device)
@@ -301,43 +399,146 @@ def run_mix(args, rank, world, local_rank):
     live_rank = int((rp_bh[h0:h1, -1] - rp_bh[h0:h1, 0]).sum())
     flops_total = pat.live_blocks() * 4 * 128 ** 3
     flops_rank = live_rank * 4 * 128 ** 3
+    steps = max(3, min(args.steps, 20))
 
     def call():
         ub.block_sparse_attn_fwd(q, k, v, rp_d, ci_d, None, out=o, lse_out=lse, plan=plan)
 
-    for _ in range(args.warmup):
+    for _ in range(3):
         call()
     torch.cuda.synchronize()
     ub.check_errors(device)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-          for _ in range(args.steps)]
+          for _ in range(steps)]
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
-    with ClockSampler(local_rank) as clk:
-        for a, b in ev:
-            a.record()
-            call()
-            b.record()
-        torch.cuda.synchronize()
-    if world > 1:
-        dist.barrier()
-    ub.check_errors(device)
-    total_ms = sum(a.elapsed_time(b) for a, b in ev)
-    t = torch.tensor([total_ms], device=device, dtype=torch.float64)
+    for a, b in ev:
+        a.record()
+        call()
+        b.record()
+    torch.cuda.synchronize()
+    rank_ms = sum(a.elapsed_time(b) for a, b in ev) / steps
+    t = torch.tensor([rank_ms], device=device, dtype=torch.float64)
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item()) / args.steps
-    rank_ms = total_ms / args.steps
+    ms = float(t.item())
 
+    # ---- pipelined: chunked kernels with the gather to rank 0 overlapped
+    chunk_plans = {}
+    for c in range(MIX_CHUNKS):
+        a, b = shard.chunk_range(n, MIX_CHUNKS, c)
+        if b > a:
+            chunk_plans[c] = ub.make_plan(rp[a:b], ci[a:b], b - a, 1, MIX_T, device=device)
+    root_out = torch.empty((total_heads, MIX_T, D), device=device, dtype=torch.float16) \
+        if rank == 0 else None
+    local_out = o.reshape(n, MIX_T, D) if rank != 0 else None
+    comm = torch.cuda.Stream(device)
+    cur = torch.cuda.current_stream(device)
+
+    def compute_chunk(c, a, b, dst):
+        ub.block_sparse_attn_fwd(q[a:b], k[a:b], v[a:b], rp_d[a:b], ci_d[a:b], None,
+                                 out=dst.view(b - a, 1, MIX_T, D), lse_out=lse[a:b],
+                                 plan=chunk_plans[c])
+
+    def pipelined():
+        works = shard.compute_and_gather(compute_chunk, MIX_CHUNKS, total_heads, world, rank,
+                                         root_out, local_out, comm_stream=comm)
+        cur.wait_stream(comm)
+        return works
+
+    for _ in range(2):  # warm-up: creates the point-to-point communicators
+        for w in pipelined():
+            w.wait()
+        torch.cuda.synchronize()
+    p_steps = max(3, min(args.steps, 10))
+    pev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(p_steps)]
+    p_ms = []
+    for a, b in pev:
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a.record()
+        works = pipelined()
+        b.record()
+        for w in works:
+            w.wait()
+        torch.cuda.synchronize()
+        p_ms.append(a.elapsed_time(b))
+    tp = torch.tensor([sum(p_ms) / p_steps], device=device, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(tp, op=dist.ReduceOp.MAX)
+    pipe_ms = float(tp.item())
+    ub.check_errors(device)
+
+    # ---- rank 0 checks the gathered rows of every rank's share against a local recompute
+    checked, max_diff, heads_checked = None, None, []
+    if rank == 0:
+        fq, fk, fv = [t.reshape(total_heads, 1, MIX_T, D) for t in full]
+        frp = pat.row_ptr.reshape(total_heads, 1, -1)
+        fci = pat.col_idx.reshape(total_heads, 1, -1)
+        checked, max_diff = True, 0.0
+        for r in range(world):
+            rs, re = shard.shard_range(total_heads, world, r)
+            for h in sorted({rs, re - 1}):
+                oh, _ = ub.block_sparse_attn_fwd(fq[h:h + 1], fk[h:h + 1], fv[h:h + 1],
+                                                 frp[h:h + 1].to(device), fci[h:h + 1].to(device),
+                                                 None)
+                d = (oh[0, 0].float() - root_out[h].float()).abs().max().item()
+                max_diff = max(max_diff, d)
+                checked = checked and torch.equal(oh[0, 0], root_out[h])
+                heads_checked.append(h)
+        torch.cuda.synchronize()
+        ub.check_errors(device)
+    res = {
+        "workload": "scaling mix B=4,H=32,T=32768,D=128: heads cycle window16 / prefix8+window8 / "
+                    "retrieval(2+16); 128 (batch, head) pairs split contiguously over the ranks",
+        "scaling": "strong",
+        "heads_per_rank": n,
+        "live_blocks": pat.live_blocks(),
+        "ms": ms,
+        "value": flops_total / (ms * 1e-3) / 1e12,
+        "unit": "TFLOP/s",
+        "frac_per_rank": flops_rank / (rank_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
+        "kernel_plus_gather_ms": pipe_ms,
+        "value_with_gather": flops_total / (pipe_ms * 1e-3) / 1e12,
+        "gather": ("none (one GPU)" if world == 1 else
+                   f"{MIX_CHUNKS} chunks per rank, NCCL send/recv to rank 0 overlapped with the "
+                   "next chunk's kernel, received in place (no concatenation)"),
+        "gather_checked": checked,
+        "gather_max_abs_diff": max_diff,
+        "gather_heads_checked": heads_checked,
+        "timed_steps": steps,
+    }
+    extra = dict(q=q, k=k, v=v, rp_d=rp_d, ci_d=ci_d, plan=plan, o=o, lse=lse,
+                 flops_total=flops_total, flops_rank=flops_rank, rank_ms=rank_ms, n=n, pat=pat)
+    return res, extra
+
+
+def run_mix(args, rank, world, local_rank):
+    """``--workload mix``: the scaling configuration as its own JSON line (with an end-to-end leg
+    through the public API on each rank's share)."""
+    import torch.distributed as dist
+    import usagi_b200 as ub
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    init_distributed(world, device)
+    ub.setup(device=str(device))
+    peaks = load_peaks()
+    with ClockSampler(local_rank) as clk:
+        mix, x = measure_mix(args, rank, world, device, peaks)
+    q, k, v, rp_d, ci_d, plan, o, lse = (x[key] for key in
+                                         ("q", "k", "v", "rp_d", "ci_d", "plan", "o", "lse"))
     # End to end on this rank's share: its q, k, v, CSR rows and work list up from pinned host
     # memory, the call, o and lse back, every step.
-    host_in = [x.cpu().pin_memory() for x in (q, k, v, rp_d, ci_d, plan.tensor)]
-    dev_in = [torch.empty_like(x) for x in (q, k, v, rp_d, ci_d, plan.tensor)]
+    host_in = [t.cpu().pin_memory() for t in (q, k, v, rp_d, ci_d, plan.tensor)]
+    dev_in = [torch.empty_like(t) for t in (q, k, v, rp_d, ci_d, plan.tensor)]
     host_out = (torch.empty(o.shape, dtype=o.dtype).pin_memory(),
                 torch.empty(lse.shape, dtype=lse.dtype).pin_memory())
-    h2d = sum(x.numel() * x.element_size() for x in host_in)
-    d2h = sum(x.numel() * x.element_size() for x in host_out)
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = sum(t.numel() * t.element_size() for t in host_out)
 
     def e2e_step():
         for d_, h_ in zip(dev_in, host_in):
@@ -364,53 +565,45 @@ def run_mix(args, rank, world, local_rank):
         dist.all_reduce(te, op=dist.ReduceOp.MAX)
     e2e_ms = float(te.item())
     assert torch.equal(host_out[0].to(device), o)
-
-    gather_ms = None
-    if world > 1 and not args.no_gather:
-        gather_ms = shard.timed_gather_to_root(o, world, rank, device)
-    clocks = clk.summary()
+    flops_total, flops_rank, rank_ms = x["flops_total"], x["flops_rank"], x["rank_ms"]
     line = {
         "metric": MIX_METRIC,
-        "value": flops_total / (ms * 1e-3) / 1e12,
+        "value": mix["value"],
         "unit": "TFLOP/s",
         "n_gpus": world,
-        "steps": args.steps,
-        "warmup": args.warmup,
-        "ms_per_step": ms,
+        "steps": mix["timed_steps"],
+        "warmup": 3,
+        "ms_per_step": mix["ms"],
         "higher_is_better": True,
         "scaling": "strong",
         "vs_baseline": None,
         "dtype": "f16",
         "data": "synthetic (seeded N(0,1) fp16; mixed CSR pattern, seed 1)",
         "config": {
-            "workload": "scaling mix B=4,H=32,T=32768,D=128: heads cycle window16 / "
-                        "prefix8+window8 / retrieval(2+16); one step = one call on each rank's "
-                        "share",
+            "workload": mix["workload"] + "; one step = one call on each rank's share",
             "global_batch": MIX_B, "heads": MIX_H, "seq_len": MIX_T, "head_dim": D,
-            "live_blocks": pat.live_blocks(),
-            "parallelism": f"heads split contiguously x{world} ({n} (batch, head) pairs per rank), "
-                           "no collective on the data path",
+            "live_blocks": mix["live_blocks"],
+            "parallelism": f"heads split contiguously x{world} ({x['n']} (batch, head) pairs per "
+                           "rank), no collective in the kernel-only timing",
             "l2": "inputs (3 GiB at N=1) larger than L2, no flush",
             "schedule": "balanced work list (bsattn_plan) per rank",
         },
-        "gpu_launches": args.steps,
+        "gpu_launches": mix["timed_steps"],
         "e2e": {"value": flops_total / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
                 "ms_per_step": e2e_ms, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "path": "usagi_b200.block_sparse_attn_fwd from pinned host buffers, per rank"},
-        "clocks": clocks,
+        "clocks": clk.summary(),
+        "mix": mix,
         "roofline": {
             "bound": "tensor", "kernel": "bsattn_fwd_kernel",
             "achieved": flops_rank / (rank_ms * 1e-3) / 1e12, "peak": peaks["bf16_tflops"],
             "peak_source": peaks["source"] + " bf16 dense burst (fp16 runs at the same rate)",
             "unit": "TFLOP/s",
             "frac": flops_rank / (rank_ms * 1e-3) / 1e12 / peaks["bf16_tflops"],
-            "algorithmic": "live tiles x 4*128^3 FLOP of rank 0's share per launch",
+            "algorithmic": "live tiles x 4*128^3 FLOP of this rank's share per launch",
             "traffic": None,
         },
     }
-    if gather_ms is not None:
-        line["gather_ms"] = gather_ms
-        line["kernel_plus_gather_ms"] = ms + gather_ms
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -540,8 +733,13 @@ def measure_e2e(ub, inputs, outs, lses, flops_step, device, world, args):
     e2e_value = world * flops_step / (e2e_ms * 1e-3) / 1e12
     for f in FAMILIES:  # the results that came back are the ones the device computed
         assert torch.equal(host_out[f][0].to(device), dev_out[f][0])
+    per_rank_s = e2e_ms * 1e-3
     return {"value": e2e_value, "unit": "TFLOP/s", "ms_per_step": e2e_ms,
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "h2d_GBps_per_rank": h2d / per_rank_s / 1e9,
+            "d2h_GBps_per_rank": d2h / per_rank_s / 1e9,
+            "host_copy_GBps_all_ranks": world * (h2d + d2h) / per_rank_s / 1e9,
+            "numa": numa_info(device.index),
             "path": "usagi_b200.block_sparse_attn_fwd from pinned host buffers, H2D+call+D2H "
                     "on separate streams (D2H of one family overlaps H2D of the next)"}
 
@@ -558,6 +756,8 @@ def main():
                     help="seconds of CPU work per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true")
+    ap.add_argument("--no-mix", action="store_true",
+                    help="skip the scaling-mix leg (B=4,H=32,T=32768, strong scaling) of the line")
     ap.add_argument("--no-plan", action="store_true",
                     help="round-robin item order instead of the balanced work list")
     ap.add_argument("--family", choices=FAMILIES, default=None,
@@ -574,6 +774,7 @@ def main():
     if args.quick:
         args.no_cpu_baseline = True
         args.no_gather = True
+        args.no_mix = True
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -672,6 +873,13 @@ def main():
         gather_ms = shard.timed_gather_to_root(outs[FAMILIES[0]], world, rank, device)
 
     clocks = clk.summary()
+
+    # ---------------- the scaling configuration (strong scaling, pipelined gather to rank 0)
+    mix = None
+    if not args.no_mix:
+        del flush
+        torch.cuda.empty_cache()
+        mix, _ = measure_mix(args, rank, world, device, peaks)
     line = {
         "metric": METRIC,
         "value": value,
@@ -716,11 +924,14 @@ def main():
     }
     if analytic is not None:
         line["analytic_rows"] = analytic
+    if mix is not None:
+        line["mix"] = mix
     if gather_ms is not None:
         line["gather_ms"] = gather_ms
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else os.cpu_count()
         line["cpu_baseline"] = cpu_reference_throughput(args.cpu_budget, threads)
+        line["cpu_baseline"]["config0"] = cpu_config0(threads)
     if rank == 0:
         print(json.dumps(line), flush=True)
     if world > 1:

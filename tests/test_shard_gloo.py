@@ -68,3 +68,51 @@ def test_sharded_oracle_gathers_to_full_result(world, kind):
         p.join(timeout=240)
     assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
     assert q.get(timeout=5) == 0.0
+
+
+def _pipelined_worker(rank, world, port, q, chunks):
+    import torch.distributed as dist
+    from oracle.bsattn_oracle import attn_blockwise
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        B, H, T = 1, 5, 1024  # 5 heads over 3 ranks: shards of 2, 2, 1; some chunks are empty
+        pat = P.mixed_pattern(B, H, T)
+        g = torch.Generator().manual_seed(0)
+        qq, kk, vv = [torch.randn(B, H, T, 128, generator=g).half() for _ in range(3)]
+        sq, sk, sv, srp, sci, _, (s0, s1) = shard.shard_problem(qq, kk, vv, pat.row_ptr,
+                                                               pat.col_idx, None, world, rank)
+
+        def compute_chunk(c, a, b, dst):
+            o, _ = attn_blockwise(sq[a:b], sk[a:b], sv[a:b], srp[a:b], sci[a:b], None)
+            dst.copy_(o.reshape(b - a, T, 128))
+
+        root = torch.full((B * H, T, 128), float("nan")) if rank == 0 else None
+        local = torch.empty((s1 - s0, T, 128)) if rank != 0 else None
+        works = shard.compute_and_gather(compute_chunk, chunks, B * H, world, rank, root, local)
+        for w in works:
+            w.wait()
+        if rank == 0:
+            ref, _ = attn_blockwise(qq, kk, vv, pat.row_ptr, pat.col_idx, None)
+            q.put(float((root.reshape(B, H, T, 128) - ref).abs().max()))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("chunks", [1, 2, 3])
+def test_pipelined_compute_and_gather_places_every_chunk(chunks):
+    """compute_and_gather: each rank's chunks land in their own rows of rank 0's output (rank 0's
+    own chunks computed in place), whatever the chunk count, including empty chunks."""
+    world = 3
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_pipelined_worker, args=(r, world, port, q, chunks))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    for p in procs:
+        p.join(timeout=240)
+    assert all(p.exitcode == 0 for p in procs), [p.exitcode for p in procs]
+    assert q.get(timeout=5) == 0.0

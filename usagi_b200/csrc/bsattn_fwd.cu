@@ -28,8 +28,8 @@
 //                         tensor store per 64-column half, lse, frees the O buffer
 //     The producer and MMA warps have the lowest warp ids: the warp schedulers favour them over
 //     the softmax warps that share their SMSPs, which keeps MMA issue off the critical path.
-//     The producer and MMA warps run their schedules with all 32 lanes so addresses and
-//     descriptors stay warp-uniform (the form TMA and tcgen05.mma take); lane 0 issues.
+//     The producer and the two MMA issuers run on lane 0 of their warps alone (one thread
+//     issues each TMA copy and each tcgen05.mma); the other lanes wait at the kernel's end.
 //   * Tensor memory, 512 columns x 128 lanes x 32 bit:
 //       S[b] = Q K^T (fp32) at columns 128 b, b = 0, 1;  O[b] (fp32) at columns 256 + 128 b.
 //       P (fp16, two per column) overwrites S[b]: keys 0..63 at columns +0..31 (written by WG1),

@@ -12,7 +12,8 @@ from typing import Optional, Tuple
 
 import torch
 
-__all__ = ["shard_range", "shard_problem", "gather_to_root", "timed_gather_to_root"]
+__all__ = ["shard_range", "shard_problem", "gather_to_root", "timed_gather_to_root",
+           "chunk_range", "compute_and_gather"]
 
 
 def shard_range(n: int, world: int, rank: int) -> Tuple[int, int]:
@@ -92,3 +93,64 @@ def timed_gather_to_root(o_shard: torch.Tensor, world: int, rank: int, device) -
     t = torch.tensor([e0.elapsed_time(e1)], device=device, dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     return float(t.item())
+
+
+def chunk_range(n: int, chunks: int, c: int) -> Tuple[int, int]:
+    """[start, end) of chunk c when n units are cut into `chunks` contiguous near-equal pieces
+    (empty pieces when n < chunks)."""
+    return shard_range(n, chunks, c)
+
+
+def compute_and_gather(compute_chunk, chunks: int, total_heads: int, world: int, rank: int,
+                       root_out: Optional[torch.Tensor], local_out: Optional[torch.Tensor],
+                       comm_stream=None, group=None) -> list:
+    """Compute this rank's heads chunk by chunk and stream every finished chunk to rank 0 while
+    the next one computes.
+
+    ``compute_chunk(c, a, b, dst)`` enqueues, on the current stream, the computation of heads
+    [a, b) of this rank's shard (``shard_range(total_heads, world, rank)``) into ``dst``, a
+    [b - a, ...] view.  On rank 0, ``dst`` is the matching slice of ``root_out``
+    ([total_heads, ...]): rank 0's own heads are written in place.  On the other ranks ``dst`` is
+    a slice of ``local_out`` ([n_local, ...]); once the chunk's kernel has finished, a
+    ``comm_stream`` waits for it and sends the slice to rank 0, which receives it directly into
+    its place in ``root_out`` -- no gather buffer and no concatenation.  Every rank uses the same
+    number of chunks, so chunk c of every rank travels in one NCCL group on rank 0.  Nothing
+    waits on the host; returns the communication work handles (the caller synchronises the
+    compute stream and ``comm_stream``).
+    """
+    import contextlib
+    import torch.distributed as dist
+    ref = root_out if rank == 0 else local_out
+    on_gpu = ref is not None and ref.is_cuda  # gloo (CPU tensors): no streams, same protocol
+    cur = torch.cuda.current_stream(ref.device) if on_gpu else None
+    comm = (comm_stream if comm_stream is not None else torch.cuda.Stream(ref.device)) \
+        if on_gpu else None
+    on_comm = (lambda: torch.cuda.stream(comm)) if on_gpu else contextlib.nullcontext
+    s0, s1 = shard_range(total_heads, world, rank)
+    works = []
+    for c in range(chunks):
+        a, b = chunk_range(s1 - s0, chunks, c)
+        if rank == 0:
+            dst = root_out[s0 + a:s0 + b]
+            ops = []
+            for r in range(1, world):
+                rs, re = shard_range(total_heads, world, r)
+                ra, rb = chunk_range(re - rs, chunks, c)
+                if rb > ra:
+                    ops.append(dist.P2POp(dist.irecv, root_out[rs + ra:rs + rb], r, group))
+            if ops:  # the receives do not depend on rank 0's own compute
+                with on_comm():
+                    works += dist.batch_isend_irecv(ops)
+            if b > a:
+                compute_chunk(c, a, b, dst)
+        else:
+            dst = local_out[a:b]
+            if b > a:
+                compute_chunk(c, a, b, dst)
+                if on_gpu:
+                    done = torch.cuda.Event()
+                    done.record(cur)
+                    comm.wait_event(done)
+                with on_comm():
+                    works += dist.batch_isend_irecv([dist.P2POp(dist.isend, dst, 0, group)])
+    return works
