@@ -430,11 +430,18 @@ def measure_mix(args, rank, world, device, peaks):
         a, b = shard.chunk_range(n, MIX_CHUNKS, c)
         if b > a:
             chunk_plans[c] = ub.make_plan(rp[a:b], ci[a:b], b - a, 1, MIX_T, device=device)
-    root_out = torch.empty((total_heads, MIX_T, D), device=device, dtype=torch.float16) \
-        if rank == 0 else None
     local_out = o.reshape(n, MIX_T, D) if rank != 0 else None
-    comm = torch.cuda.Stream(device)
     cur = torch.cuda.current_stream(device)
+    transport = args.mix_transport if world > 1 else "none"
+    peer = None
+    if transport == "copy":
+        peer = shard.PeerGather((total_heads, MIX_T, D), torch.float16, total_heads, world, rank,
+                                device)
+        root_out = peer.root if rank == 0 else None
+    else:
+        root_out = torch.empty((total_heads, MIX_T, D), device=device, dtype=torch.float16) \
+            if rank == 0 else None
+        comm = torch.cuda.Stream(device)
 
     def compute_chunk(c, a, b, dst):
         ub.block_sparse_attn_fwd(q[a:b], k[a:b], v[a:b], rp_d[a:b], ci_d[a:b], None,
@@ -442,12 +449,15 @@ def measure_mix(args, rank, world, device, peaks):
                                  plan=chunk_plans[c])
 
     def pipelined():
+        if peer is not None:
+            peer.run(compute_chunk, MIX_CHUNKS, local_out)
+            return []
         works = shard.compute_and_gather(compute_chunk, MIX_CHUNKS, total_heads, world, rank,
                                          root_out, local_out, comm_stream=comm)
         cur.wait_stream(comm)
         return works
 
-    for _ in range(2):  # warm-up: creates the point-to-point communicators
+    for _ in range(2):  # warm-up: creates the point-to-point communicators / peer mappings
         for w in pipelined():
             w.wait()
         torch.cuda.synchronize()
@@ -471,6 +481,8 @@ def measure_mix(args, rank, world, device, peaks):
         dist.all_reduce(tp, op=dist.ReduceOp.MAX)
     pipe_ms = float(tp.item())
     ub.check_errors(device)
+    if world > 1:
+        dist.barrier()
 
     # ---- rank 0 checks the gathered rows of every rank's share against a local recompute
     checked, max_diff, heads_checked = None, None, []
@@ -491,6 +503,8 @@ def measure_mix(args, rank, world, device, peaks):
                 heads_checked.append(h)
         torch.cuda.synchronize()
         ub.check_errors(device)
+    if peer is not None:
+        peer.close()
     res = {
         "workload": "scaling mix B=4,H=32,T=32768,D=128: heads cycle window16 / prefix8+window8 / "
                     "retrieval(2+16); 128 (batch, head) pairs split contiguously over the ranks",
@@ -504,8 +518,11 @@ def measure_mix(args, rank, world, device, peaks):
         "kernel_plus_gather_ms": pipe_ms,
         "value_with_gather": flops_total / (pipe_ms * 1e-3) / 1e12,
         "gather": ("none (one GPU)" if world == 1 else
-                   f"{MIX_CHUNKS} chunks per rank, NCCL send/recv to rank 0 overlapped with the "
-                   "next chunk's kernel, received in place (no concatenation)"),
+                   f"{MIX_CHUNKS} chunks per rank; each finished chunk copied to rank 0 while the "
+                   "next one computes, in place (no concatenation), by " +
+                   ("copy-engine peer copies over NVLink into rank 0's buffer (CUDA IPC), which "
+                    "need no SMs" if transport == "copy" else "NCCL send/recv on a second stream")),
+        "gather_transport": transport,
         "gather_checked": checked,
         "gather_max_abs_diff": max_diff,
         "gather_heads_checked": heads_checked,
@@ -756,6 +773,9 @@ def main():
                     help="seconds of CPU work per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true")
+    ap.add_argument("--mix-transport", choices=["copy", "nccl"], default="copy",
+                    help="how the scaling mix's chunks reach rank 0: copy-engine peer copies "
+                         "(default) or NCCL send/recv")
     ap.add_argument("--no-mix", action="store_true",
                     help="skip the scaling-mix leg (B=4,H=32,T=32768, strong scaling) of the line")
     ap.add_argument("--no-plan", action="store_true",

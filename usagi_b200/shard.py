@@ -13,7 +13,7 @@ from typing import Optional, Tuple
 import torch
 
 __all__ = ["shard_range", "shard_problem", "gather_to_root", "timed_gather_to_root",
-           "chunk_range", "compute_and_gather"]
+           "chunk_range", "compute_and_gather", "PeerGather"]
 
 
 def shard_range(n: int, world: int, rank: int) -> Tuple[int, int]:
@@ -154,3 +154,85 @@ def compute_and_gather(compute_chunk, chunks: int, total_heads: int, world: int,
                 with on_comm():
                     works += dist.batch_isend_irecv([dist.P2POp(dist.isend, dst, 0, group)])
     return works
+
+
+class PeerGather:
+    """Rank 0's [total_heads, ...] output buffer, written by every rank with copy-engine peer
+    copies.
+
+    Why not NCCL for the overlapped gather: NCCL moves data with kernels, and the attention
+    kernel is persistent -- one CTA per SM holding the whole register file and 227 KB of shared
+    memory -- so an NCCL kernel queued on another stream only runs between attention launches.
+    A peer ``copy_`` between two GPUs is a DMA on a copy engine and needs no SM, so it runs while
+    the next chunk computes.  Rank 0 exports its buffer once with CUDA IPC (torch's CUDA tensor
+    sharing); every other rank maps it and copies each finished chunk straight into its rows
+    over NVLink.  Completion reaches rank 0 through one interprocess CUDA event per rank, which
+    rank 0's stream waits on after a host barrier (gloo) that orders the event records before
+    the waits.  Construct collectively on every rank (after the NCCL process group exists).
+    """
+
+    def __init__(self, shape, dtype, total_heads: int, world: int, rank: int, device):
+        import torch.distributed as dist
+        from torch.multiprocessing.reductions import rebuild_cuda_tensor, reduce_tensor
+        self.world, self.rank, self.total_heads = world, rank, total_heads
+        self.device = torch.device(device)
+        self.host = dist.new_group(backend="gloo")  # host-side ordering only
+        obj = [None]
+        if rank == 0:
+            self.root = torch.empty(shape, dtype=dtype, device=self.device)
+            obj = [reduce_tensor(self.root)[1]]
+        dist.broadcast_object_list(obj, src=0, group=self.host)
+        handle = None
+        self.event = None
+        if rank != 0:
+            with torch.cuda.device(self.device):
+                self.root = rebuild_cuda_tensor(*obj[0])  # rank 0's memory, mapped here
+                self.event = torch.cuda.Event(interprocess=True)
+                self.event.record(torch.cuda.current_stream(self.device))
+                handle = self.event.ipc_handle()
+        handles = [None] * world
+        dist.all_gather_object(handles, handle, group=self.host)
+        self.peer_events = []
+        if rank == 0:
+            with torch.cuda.device(self.device):
+                self.peer_events = [torch.cuda.Event.from_ipc_handle(self.device, h)
+                                    for h in handles[1:]]
+        self.comm = torch.cuda.Stream(self.device)
+
+    def run(self, compute_chunk, chunks: int, local_out: Optional[torch.Tensor]) -> None:
+        """One compute + gather: ``compute_chunk(c, a, b, dst)`` as in ``compute_and_gather``.
+        Rank 0 computes into its rows of ``self.root``; the other ranks compute into
+        ``local_out`` and push each finished chunk to rank 0 on the copy stream.  On return,
+        rank 0's current stream is ordered after every rank's copies (it has waited on their
+        events); the other ranks' current streams are ordered after their own copies."""
+        import torch.distributed as dist
+        cur = torch.cuda.current_stream(self.device)
+        s0, s1 = shard_range(self.total_heads, self.world, self.rank)
+        for c in range(chunks):
+            a, b = chunk_range(s1 - s0, chunks, c)
+            if b <= a:
+                continue
+            if self.rank == 0:
+                compute_chunk(c, a, b, self.root[s0 + a:s0 + b])
+                continue
+            compute_chunk(c, a, b, local_out[a:b])
+            done = torch.cuda.Event()
+            done.record(cur)
+            self.comm.wait_event(done)
+            with torch.cuda.stream(self.comm):
+                self.root[s0 + a:s0 + b].copy_(local_out[a:b], non_blocking=True)
+        if self.rank != 0:
+            self.event.record(self.comm)
+            cur.wait_stream(self.comm)
+        dist.barrier(group=self.host)  # every rank has recorded its event
+        if self.rank == 0:
+            for ev in self.peer_events:
+                cur.wait_event(ev)
+
+    def close(self) -> None:
+        """Unmap rank 0's buffer on the other ranks before rank 0 frees it (collective)."""
+        import torch.distributed as dist
+        torch.cuda.synchronize(self.device)
+        if self.rank != 0:
+            self.root = None
+        dist.barrier(group=self.host)
