@@ -185,6 +185,24 @@ BSATTN_API int bsattn_build_csr(int kind, int nqb, int prefix, int window, int n
                                 uint64_t seed, int n_heads, int32_t* row_ptr, int32_t* col_idx,
                                 int64_t ci_stride, void* stream);
 
+/* Peer-memory plumbing for gathering o shards onto one GPU (one process per GPU).  No counterpart
+ * in the reference, which has no multi-GPU code.  The attention kernel is persistent and occupies
+ * every SM, so a gather that runs while it computes must not need SMs: these let each rank copy
+ * its finished heads straight into the root rank's output buffer with the copy engines (a DMA
+ * over NVLink).
+ *   bsattn_ipc_export: CUDA IPC handle (BSATTN_IPC_HANDLE_BYTES bytes into `handle`) of the
+ *     allocation holding device pointer `ptr`, and ptr's byte offset inside that allocation.
+ *   bsattn_ipc_open: maps an exported allocation into the CURRENT device's context (peer access
+ *     enabled) and returns the mapped address of base + offset in *ptr; one open per handle and
+ *     process.  bsattn_ipc_close takes that same pointer and the same offset.
+ *   bsattn_peer_copy: enqueues a copy of `bytes` from src to dst on `stream` (either may be a
+ *     mapped peer address); no SM work for a device-to-peer copy. */
+#define BSATTN_IPC_HANDLE_BYTES 64
+BSATTN_API int bsattn_ipc_export(const void* ptr, void* handle, uint64_t* offset);
+BSATTN_API int bsattn_ipc_open(const void* handle, uint64_t offset, void** ptr);
+BSATTN_API int bsattn_ipc_close(void* ptr, uint64_t offset);
+BSATTN_API int bsattn_peer_copy(void* dst, const void* src, size_t bytes, void* stream);
+
 /* Human-readable text for a BSATTN_E* code. */
 BSATTN_API const char* bsattn_strerror(int code);
 

@@ -59,6 +59,10 @@ SIGNATURES = {
                                 ctypes.POINTER(ctypes.c_int64)]),
     "bsattn_build_csr": (_c_int, [_c_int, _c_int, _c_int, _c_int, _c_int, ctypes.c_uint64,
                                   _c_int, _c_void_p, _c_void_p, ctypes.c_int64, _c_void_p]),
+    "bsattn_ipc_export": (_c_int, [_c_void_p, _c_void_p, ctypes.POINTER(ctypes.c_uint64)]),
+    "bsattn_ipc_open": (_c_int, [_c_void_p, ctypes.c_uint64, ctypes.POINTER(_c_void_p)]),
+    "bsattn_ipc_close": (_c_int, [_c_void_p, ctypes.c_uint64]),
+    "bsattn_peer_copy": (_c_int, [_c_void_p, _c_void_p, _c_size_t, _c_void_p]),
     "bsattn_fwd_noalloc": (_c_int, [
         _c_void_p, _c_void_p, _c_void_p,          # q, k, v
         _c_void_p, _c_void_p,                     # o, lse

@@ -24,7 +24,7 @@ LIB_PATH = PKG_DIR / LIB_NAME
 # Hash of the sources, headers and flags the in-tree library was built from (written next to it).
 STAMP_PATH = PKG_DIR / (LIB_NAME + ".sha256")
 
-SOURCES = ["bsattn_fwd.cu", "csr_build.cu"]
+SOURCES = ["bsattn_fwd.cu", "csr_build.cu", "peer.cu"]
 HEADERS = ["sm100_ptx.cuh"]
 
 NVCC_FLAGS = [

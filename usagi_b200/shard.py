@@ -161,32 +161,52 @@ class PeerGather:
     copies.
 
     Why not NCCL for the overlapped gather: NCCL moves data with kernels, and the attention
-    kernel is persistent -- one CTA per SM holding the whole register file and 227 KB of shared
+    kernel is persistent -- one CTA per SM holding the whole register file and most of shared
     memory -- so an NCCL kernel queued on another stream only runs between attention launches.
-    A peer ``copy_`` between two GPUs is a DMA on a copy engine and needs no SM, so it runs while
-    the next chunk computes.  Rank 0 exports its buffer once with CUDA IPC (torch's CUDA tensor
-    sharing); every other rank maps it and copies each finished chunk straight into its rows
-    over NVLink.  Completion reaches rank 0 through one interprocess CUDA event per rank, which
-    rank 0's stream waits on after a host barrier (gloo) that orders the event records before
-    the waits.  Construct collectively on every rank (after the NCCL process group exists).
+    A device-to-peer copy is a DMA on a copy engine and needs no SM, so it runs while the next
+    chunk computes.  Rank 0 exports its buffer once with CUDA IPC (bsattn_ipc_export); every
+    other rank maps it into its own device's context (bsattn_ipc_open, peer access over NVLink)
+    and copies each finished chunk straight into its rows (bsattn_peer_copy).  Completion reaches
+    rank 0 through one interprocess CUDA event per rank, which rank 0's stream waits on after a
+    host barrier (gloo) that orders the event records before the waits.  Construct collectively
+    on every rank after the NCCL process group exists; ``close`` collectively before freeing.
     """
 
     def __init__(self, shape, dtype, total_heads: int, world: int, rank: int, device):
+        import ctypes
         import torch.distributed as dist
-        from torch.multiprocessing.reductions import rebuild_cuda_tensor, reduce_tensor
+        from . import _lib
+        self.lib = _lib.load()
         self.world, self.rank, self.total_heads = world, rank, total_heads
         self.device = torch.device(device)
         self.host = dist.new_group(backend="gloo")  # host-side ordering only
+        self.row_bytes = 1
+        for d in shape[1:]:
+            self.row_bytes *= int(d)
+        self.row_bytes *= torch.empty((), dtype=dtype).element_size()
         obj = [None]
+        self.root = None
+        self.remote = None  # rank != 0: mapped address of rank 0's buffer
         if rank == 0:
             self.root = torch.empty(shape, dtype=dtype, device=self.device)
-            obj = [reduce_tensor(self.root)[1]]
+            handle = ctypes.create_string_buffer(64)
+            off = ctypes.c_uint64(0)
+            with torch.cuda.device(self.device):
+                rc = self.lib.bsattn_ipc_export(self.root.data_ptr(), handle, ctypes.byref(off))
+            if rc != 0:
+                raise RuntimeError(f"bsattn_ipc_export: {_lib.strerror(rc)}")
+            obj = [(handle.raw, off.value)]
         dist.broadcast_object_list(obj, src=0, group=self.host)
         handle = None
         self.event = None
         if rank != 0:
+            raw, self.offset = obj[0]
+            ptr = ctypes.c_void_p(0)
             with torch.cuda.device(self.device):
-                self.root = rebuild_cuda_tensor(*obj[0])  # rank 0's memory, mapped here
+                rc = self.lib.bsattn_ipc_open(raw, self.offset, ctypes.byref(ptr))
+                if rc != 0:
+                    raise RuntimeError(f"bsattn_ipc_open: {_lib.strerror(rc)}")
+                self.remote = ptr.value
                 self.event = torch.cuda.Event(interprocess=True)
                 self.event.record(torch.cuda.current_stream(self.device))
                 handle = self.event.ipc_handle()
@@ -202,10 +222,11 @@ class PeerGather:
     def run(self, compute_chunk, chunks: int, local_out: Optional[torch.Tensor]) -> None:
         """One compute + gather: ``compute_chunk(c, a, b, dst)`` as in ``compute_and_gather``.
         Rank 0 computes into its rows of ``self.root``; the other ranks compute into
-        ``local_out`` and push each finished chunk to rank 0 on the copy stream.  On return,
-        rank 0's current stream is ordered after every rank's copies (it has waited on their
-        events); the other ranks' current streams are ordered after their own copies."""
+        ``local_out`` (contiguous [n_local, ...]) and push each finished chunk to rank 0 on the
+        copy stream.  On return rank 0's current stream is ordered after every rank's copies (it
+        waited on their events); the other ranks' current streams after their own copies."""
         import torch.distributed as dist
+        from . import _lib
         cur = torch.cuda.current_stream(self.device)
         s0, s1 = shard_range(self.total_heads, self.world, self.rank)
         for c in range(chunks):
@@ -215,12 +236,15 @@ class PeerGather:
             if self.rank == 0:
                 compute_chunk(c, a, b, self.root[s0 + a:s0 + b])
                 continue
-            compute_chunk(c, a, b, local_out[a:b])
+            src = local_out[a:b]
+            compute_chunk(c, a, b, src)
             done = torch.cuda.Event()
             done.record(cur)
             self.comm.wait_event(done)
-            with torch.cuda.stream(self.comm):
-                self.root[s0 + a:s0 + b].copy_(local_out[a:b], non_blocking=True)
+            rc = self.lib.bsattn_peer_copy(self.remote + (s0 + a) * self.row_bytes, src.data_ptr(),
+                                           (b - a) * self.row_bytes, self.comm.cuda_stream)
+            if rc != 0:
+                raise RuntimeError(f"bsattn_peer_copy: {_lib.strerror(rc)}")
         if self.rank != 0:
             self.event.record(self.comm)
             cur.wait_stream(self.comm)
@@ -230,9 +254,11 @@ class PeerGather:
                 cur.wait_event(ev)
 
     def close(self) -> None:
-        """Unmap rank 0's buffer on the other ranks before rank 0 frees it (collective)."""
+        """Unmap rank 0's buffer on the other ranks before rank 0 may free it (collective)."""
         import torch.distributed as dist
         torch.cuda.synchronize(self.device)
-        if self.rank != 0:
-            self.root = None
+        if self.rank != 0 and self.remote is not None:
+            with torch.cuda.device(self.device):
+                self.lib.bsattn_ipc_close(self.remote, self.offset)
+            self.remote = None
         dist.barrier(group=self.host)
