@@ -8,15 +8,21 @@ summed over the three calls and all ranks, divided by the max-over-ranks device 
 
 Multi-GPU: one process per GPU (torchrun); every rank runs the same per-GPU workload on its own
 (batch, head) shard -- B = 2 per rank of a global batch 2N -- with no collective on the data path
-(weak scaling).  The optional NCCL gather of o to rank 0 is timed separately (``gather_ms``).
+(weak scaling).  The optional NCCL gather of one family's o to rank 0 is timed separately
+(``gather_ms``).
+
+Every line also carries ``mix``: the head-sharded scaling configuration, one B=4, H=32, T=32768
+problem whose heads cycle through window16 / prefix8+window8 / retrieval(2+16), its 128 (batch,
+head) pairs split contiguously across the N ranks (strong scaling: the total work is fixed).  It
+reports the kernel time (max over ranks) and the time until rank 0 holds every head, with each
+rank's heads computed in chunks and every finished chunk copied into rank 0's output while the
+next one computes (copy-engine peer copies over NVLink; NCCL send/recv with --mix-transport nccl),
+and rank 0's bit-exact check of the first and last head of every rank's share.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload families|mix]
+                    [--workload families|mix] [--mix-transport copy|nccl] [--no-mix]
 
-``--workload mix`` measures the head-sharded scaling configuration instead: one B=4, H=32,
-T=32768 problem whose heads cycle through window16 / prefix8+window8 / retrieval(2+16), its 128
-(batch, head) pairs split contiguously across the N ranks (strong scaling: the total work is
-fixed), o gathered to rank 0 over NCCL and timed separately.
+``--workload mix`` prints the scaling configuration as its own line (with an end-to-end leg).
 
 ``--impl reference`` times the reference's CPU path (the dense-masked fp32 restatement in
 oracle/, the reference having no CPU implementation of its own) on the host cores, rank 0 only.
@@ -434,9 +440,14 @@ def measure_mix(args, rank, world, device, peaks):
     cur = torch.cuda.current_stream(device)
     transport = args.mix_transport if world > 1 else "none"
     peer = None
+    fallback = None
     if transport == "copy":
-        peer = shard.PeerGather((total_heads, MIX_T, D), torch.float16, total_heads, world, rank,
-                                device)
+        try:
+            peer = shard.PeerGather((total_heads, MIX_T, D), torch.float16, total_heads, world,
+                                    rank, device)
+        except shard.PeerGatherUnavailable as e:  # raised on every rank together
+            fallback, transport = str(e), "nccl"
+    if peer is not None:
         root_out = peer.root if rank == 0 else None
     else:
         root_out = torch.empty((total_heads, MIX_T, D), device=device, dtype=torch.float16) \
@@ -523,6 +534,7 @@ def measure_mix(args, rank, world, device, peaks):
                    ("copy-engine peer copies over NVLink into rank 0's buffer (CUDA IPC), which "
                     "need no SMs" if transport == "copy" else "NCCL send/recv on a second stream")),
         "gather_transport": transport,
+        "gather_fallback_reason": fallback,
         "gather_checked": checked,
         "gather_max_abs_diff": max_diff,
         "gather_heads_checked": heads_checked,

@@ -13,7 +13,8 @@ from typing import Optional, Tuple
 import torch
 
 __all__ = ["shard_range", "shard_problem", "gather_to_root", "timed_gather_to_root",
-           "chunk_range", "compute_and_gather", "PeerGather"]
+           "chunk_range", "compute_and_gather", "PeerGather",
+           "PeerGatherUnavailable"]
 
 
 def shard_range(n: int, world: int, rank: int) -> Tuple[int, int]:
@@ -156,6 +157,11 @@ def compute_and_gather(compute_chunk, chunks: int, total_heads: int, world: int,
     return works
 
 
+class PeerGatherUnavailable(RuntimeError):
+    """Raised on every rank when any rank could not map rank 0's buffer (the caller falls back to
+    a kernel-based gather)."""
+
+
 class PeerGather:
     """Rank 0's [total_heads, ...] output buffer, written by every rank with copy-engine peer
     copies.
@@ -187,36 +193,54 @@ class PeerGather:
         obj = [None]
         self.root = None
         self.remote = None  # rank != 0: mapped address of rank 0's buffer
+        self.event = None
+        err = ""
         if rank == 0:
-            self.root = torch.empty(shape, dtype=dtype, device=self.device)
-            handle = ctypes.create_string_buffer(64)
-            off = ctypes.c_uint64(0)
-            with torch.cuda.device(self.device):
-                rc = self.lib.bsattn_ipc_export(self.root.data_ptr(), handle, ctypes.byref(off))
-            if rc != 0:
-                raise RuntimeError(f"bsattn_ipc_export: {_lib.strerror(rc)}")
-            obj = [(handle.raw, off.value)]
+            try:
+                self.root = torch.empty(shape, dtype=dtype, device=self.device)
+                handle = ctypes.create_string_buffer(64)
+                off = ctypes.c_uint64(0)
+                with torch.cuda.device(self.device):
+                    rc = self.lib.bsattn_ipc_export(self.root.data_ptr(), handle, ctypes.byref(off))
+                if rc != 0:
+                    raise RuntimeError(f"bsattn_ipc_export: {_lib.strerror(rc)}")
+                obj = [(handle.raw, off.value)]
+            except Exception as e:  # noqa: BLE001 -- reported to every rank below
+                err = f"rank 0: {e}"
         dist.broadcast_object_list(obj, src=0, group=self.host)
         handle = None
-        self.event = None
-        if rank != 0:
-            raw, self.offset = obj[0]
-            ptr = ctypes.c_void_p(0)
-            with torch.cuda.device(self.device):
-                rc = self.lib.bsattn_ipc_open(raw, self.offset, ctypes.byref(ptr))
-                if rc != 0:
-                    raise RuntimeError(f"bsattn_ipc_open: {_lib.strerror(rc)}")
-                self.remote = ptr.value
-                self.event = torch.cuda.Event(interprocess=True)
-                self.event.record(torch.cuda.current_stream(self.device))
-                handle = self.event.ipc_handle()
-        handles = [None] * world
-        dist.all_gather_object(handles, handle, group=self.host)
+        if rank != 0 and obj[0] is not None:
+            try:
+                raw, self.offset = obj[0]
+                ptr = ctypes.c_void_p(0)
+                with torch.cuda.device(self.device):
+                    rc = self.lib.bsattn_ipc_open(raw, self.offset, ctypes.byref(ptr))
+                    if rc != 0:
+                        raise RuntimeError(f"bsattn_ipc_open: {_lib.strerror(rc)}")
+                    self.remote = ptr.value
+                    self.event = torch.cuda.Event(interprocess=True)
+                    self.event.record(torch.cuda.current_stream(self.device))
+                    handle = self.event.ipc_handle()
+            except Exception as e:  # noqa: BLE001
+                err = f"rank {rank}: {e}"
+        elif rank != 0:
+            err = f"rank {rank}: no handle from rank 0"
+        # Every rank learns whether every rank is set up, so all take the same path.
+        status = [None] * world
+        dist.all_gather_object(status, (err, handle), group=self.host)
+        errors = [e for e, _ in status if e]
+        if errors:
+            if self.remote is not None:
+                with torch.cuda.device(self.device):
+                    self.lib.bsattn_ipc_close(self.remote, self.offset)
+                self.remote = None
+            dist.barrier(group=self.host)
+            raise PeerGatherUnavailable("; ".join(errors))
         self.peer_events = []
         if rank == 0:
             with torch.cuda.device(self.device):
                 self.peer_events = [torch.cuda.Event.from_ipc_handle(self.device, h)
-                                    for h in handles[1:]]
+                                    for _, h in status[1:]]
         self.comm = torch.cuda.Stream(self.device)
 
     def run(self, compute_chunk, chunks: int, local_out: Optional[torch.Tensor]) -> None:
