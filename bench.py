@@ -370,10 +370,13 @@ def measure_mix(args, rank, world, device, peaks):
     One B=4, H=32, T=32768 problem (heads cycle window16 / prefix8+window8 / retrieval 2+16); its
     128 (batch, head) pairs are split contiguously across the ranks.  Two measurements:
       * kernel: one call per rank on its whole share; ms = max over ranks of the device time;
-      * pipelined: each rank's share computed in MIX_CHUNKS chunks, each finished chunk sent to
-        rank 0 (NCCL point-to-point on a second stream) while the next one computes, received in
-        place into rank 0's [B*H, T, D] output; ms = max over ranks from the first launch until
-        rank 0 holds every head.  At N = 1 there is nothing to send: the chunked kernels alone.
+      * kernel + gather: ms = max over ranks from the first launch until rank 0 holds every
+        head in its [B*H, T, D] output.  With the default transport (fused) each rank runs one
+        kernel whose epilogue stores its output tiles straight into its rows of rank 0's buffer
+        (CUDA IPC mapping), so the transfer overlaps the computation tile by tile.  The other
+        transports compute each share in MIX_CHUNKS chunks and move every finished chunk while
+        the next one computes: copy-engine peer copies (copy) or NCCL send/recv (nccl).  At
+        N = 1 there is nothing to send: the chunked kernels alone.
     Rank 0 then recomputes the first and last head of every rank's share on its own GPU and
     checks that the gathered rows equal them bit for bit.  Returns (dict, extra) where extra
     holds the tensors the standalone mix line needs for its end-to-end leg.
@@ -440,7 +443,7 @@ def measure_mix(args, rank, world, device, peaks):
     transport = args.mix_transport if world > 1 else "none"
     peer = None
     fallback = None
-    if transport == "copy":
+    if transport in ("copy", "fused"):
         try:
             peer = shard.PeerGather((total_heads, MIX_T, D), torch.float16, total_heads, world,
                                     rank, device)
@@ -459,6 +462,10 @@ def measure_mix(args, rank, world, device, peaks):
                                  plan=chunk_plans[c])
 
     def pipelined():
+        if peer is not None and transport == "fused":
+            peer.run_fused(lambda ptr: ub.block_sparse_attn_fwd_into(
+                ptr, q, k, v, rp_d, ci_d, None, lse_out=lse, plan=plan))
+            return []
         if peer is not None:
             peer.run(compute_chunk, MIX_CHUNKS, local_out)
             return []
@@ -528,6 +535,10 @@ def measure_mix(args, rank, world, device, peaks):
         "kernel_plus_gather_ms": pipe_ms,
         "value_with_gather": flops_total / (pipe_ms * 1e-3) / 1e12,
         "gather": ("none (one GPU)" if world == 1 else
+                   "one kernel per rank whose epilogue stores every output tile straight into "
+                   "rank 0's buffer over NVLink (CUDA IPC mapping, TMA tensor stores), so the "
+                   "transfer overlaps the computation tile by tile; no copy follows"
+                   if transport == "fused" else
                    f"{MIX_CHUNKS} chunks per rank; each finished chunk copied to rank 0 while the "
                    "next one computes, in place (no concatenation), by " +
                    ("copy-engine peer copies over NVLink into rank 0's buffer (CUDA IPC), which "
@@ -818,9 +829,11 @@ def main():
                     help="seconds of CPU work per reference-arm step")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-gather", action="store_true")
-    ap.add_argument("--mix-transport", choices=["copy", "nccl"], default="copy",
-                    help="how the scaling mix's chunks reach rank 0: copy-engine peer copies "
-                         "(default) or NCCL send/recv")
+    ap.add_argument("--mix-transport", choices=["fused", "copy", "nccl"], default="fused",
+                    help="how the scaling mix's output reaches rank 0: fused (default; each "
+                         "rank's kernel stores its tiles straight into rank 0's buffer), copy "
+                         "(copy-engine peer copies of finished chunks) or nccl (send/recv of "
+                         "chunks)")
     ap.add_argument("--no-mix", action="store_true",
                     help="skip the scaling-mix leg (B=4,H=32,T=32768, strong scaling) of the line")
     ap.add_argument("--no-plan", action="store_true",

@@ -1,13 +1,14 @@
 """shard.PeerGather on one GPU: two processes play rank 0 and rank 1 (gloo for the host side).
 
 Rank 0 exports its output buffer through the library's IPC entry points; rank 1 maps it into its
-own context and copies its finished chunks into rank 0's rows with copy-engine copies; rank 0's
-stream waits on rank 1's interprocess event.  Both ranks compute their heads with the attention
-kernel.  Rank 0 then checks every head of the gathered output against its own single-process
-computation of the whole problem, bit for bit.  On one GPU the copies are device-to-device within
-the same memory, but the code path (export, open in the copying process's context, peer copy,
-event ordering, close) is the one the multi-GPU gather runs.  Nothing in either process waits on
-the other inside a kernel: only copies and events are shared.
+own context.  Either rank 1 copies its finished chunks into rank 0's rows with copy-engine copies
+(``run``), or rank 1's attention kernel writes its output tiles straight into those rows
+(``run_fused`` with ``block_sparse_attn_fwd_into``).  Rank 0's stream waits on rank 1's
+interprocess event.  Rank 0 then checks every head of the gathered output against its own
+single-process computation of the whole problem, bit for bit.  On one GPU the writes stay in the
+same memory, but the code path (export, open in the writing process's context, copies or kernel
+stores through the mapping, event ordering, close) is the one the multi-GPU gather runs.  Nothing
+in either process waits on the other inside a kernel: only memory and events are shared.
 """
 import os
 import socket
@@ -27,7 +28,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, q, chunks):
+def _worker(rank, world, port, q, mode, chunks):
     import torch.distributed as dist
     import usagi_b200 as ub
     from usagi_b200 import patterns as P
@@ -62,7 +63,11 @@ def _worker(rank, world, port, q, chunks):
                 peer.root.fill_(float("nan"))
             torch.cuda.synchronize()
             dist.barrier()
-            peer.run(compute_chunk, chunks, local)
+            if mode == "fused":
+                peer.run_fused(lambda ptr: ub.block_sparse_attn_fwd_into(
+                    ptr, sq, sk, sv, srp, sci, None, lse_out=lse))
+            else:
+                peer.run(compute_chunk, chunks, local)
             torch.cuda.synchronize()
             dist.barrier()
             if rank == 0:
@@ -77,12 +82,12 @@ def _worker(rank, world, port, q, chunks):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("chunks", [1, 2])
-def test_peer_gather_two_processes_one_gpu(chunks):
+@pytest.mark.parametrize("mode,chunks", [("copy", 1), ("copy", 2), ("fused", 1)])
+def test_peer_gather_two_processes_one_gpu(mode, chunks):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, chunks)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, mode, chunks)) for r in range(2)]
     for p in procs:
         p.start()
     for p in procs:

@@ -9,6 +9,7 @@ from .api import (  # noqa: F401
     BsattnError,
     Plan,
     block_sparse_attn_fwd,
+    block_sparse_attn_fwd_into,
     block_sparse_attn_fwd_window,
     make_plan,
     make_window_plan,

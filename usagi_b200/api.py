@@ -189,8 +189,10 @@ def _build_plan(B, H, T, seq_lens, device, grid, name, fill) -> Plan:
     return Plan(host.to(dev), grid, B, H, T)
 
 
-def _prepare(q, k, v, seq_lens, out_dtype, out, lse_out, return_lse):
-    """Shared checks and buffers of the entry points: (q, k, v, flags, seq_lens, o, lse)."""
+def _prepare(q, k, v, seq_lens, out_dtype, out, lse_out, return_lse, alloc_out=True):
+    """Shared checks and buffers of the entry points: (q, k, v, flags, seq_lens, o, lse).
+    With ``alloc_out=False`` no o is checked or allocated (o is None): the caller supplies its
+    device address."""
     lib = _lib.load()
     if q.dim() != 4:
         raise ValueError(f"q must be [B, H, T, D], got {tuple(q.shape)}")
@@ -225,7 +227,9 @@ def _prepare(q, k, v, seq_lens, out_dtype, out, lse_out, return_lse):
         sl = seq_lens.to(device=dev, dtype=torch.int32).contiguous()
         if sl.numel() != B:
             raise ValueError(f"seq_lens: expected {B} entries, got {sl.numel()}")
-    if out is None:
+    if not alloc_out:
+        out = None
+    elif out is None:
         out = torch.empty((B, H, T, D), device=dev, dtype=out_dtype)
     elif out.shape != (B, H, T, D) or out.dtype != out_dtype or not out.is_contiguous():
         raise ValueError("out has the wrong shape, dtype or layout")
@@ -267,9 +271,17 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     [B, H, T] (None if ``return_lse=False``).  ``plan`` (from :func:`make_plan` for this pattern)
     balances the work across the persistent CTAs; results are identical with or without it.
     """
+    return _fwd_csr(q, k, v, row_ptr, col_idx, seq_lens, scale, out_dtype, out, lse_out,
+                    return_lse, plan, None)
+
+
+def _fwd_csr(q, k, v, row_ptr, col_idx, seq_lens, scale, out_dtype, out, lse_out, return_lse,
+             plan, out_ptr):
+    """The CSR call (``bsattn_fwd_plan``); o goes to ``out`` or, when ``out_ptr`` is given, to
+    that device address."""
     lib = _lib.load()
     q, k, v, flags, sl, out, lse = _prepare(q, k, v, seq_lens, out_dtype, out, lse_out,
-                                            return_lse)
+                                            return_lse, alloc_out=out_ptr is None)
     B, H, T, D = q.shape
     dev = q.device
     nqb = T // BLOCK_SIZE
@@ -283,7 +295,8 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
         ws = _workspace(dev, stream)
         plan_ptr, plan_grid = _plan_args(plan, B, H, T, dev)
         rc = lib.bsattn_fwd_plan(
-            q.data_ptr(), k.data_ptr(), v.data_ptr(), out.data_ptr(),
+            q.data_ptr(), k.data_ptr(), v.data_ptr(),
+            out.data_ptr() if out is not None else out_ptr,
             lse.data_ptr() if lse is not None else None,
             rp.data_ptr(), ci.data_ptr(), sl.data_ptr() if sl is not None else None,
             B, H, T, D, rp_stride, ci_stride, max_nnz,
@@ -292,6 +305,28 @@ def block_sparse_attn_fwd(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
     if rc != 0:
         raise BsattnError(rc, "bsattn_fwd")
     return out, lse
+
+
+def block_sparse_attn_fwd_into(o_ptr: int, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,
+                               row_ptr: torch.Tensor, col_idx: torch.Tensor,
+                               seq_lens: Optional[torch.Tensor] = None, *,
+                               scale: Optional[float] = None,
+                               out_dtype: Optional[torch.dtype] = None,
+                               lse_out: Optional[torch.Tensor] = None,
+                               return_lse: bool = True,
+                               plan: Optional[Plan] = None):
+    """:func:`block_sparse_attn_fwd` writing o to the device address ``o_ptr`` instead of a
+    tensor: contiguous [B, H, T, 128] in ``out_dtype``, 16-byte aligned, reachable from q's GPU.
+    That may be another GPU's buffer mapped into this process (CUDA IPC with peer access, as
+    :class:`usagi_b200.shard.PeerGather` sets up): the kernel's tile stores then cross NVLink as
+    each tile is finished, with no copy afterwards.  Returns lse (None if ``return_lse=False``).
+    The call is ordered on the current stream like the tensor entry point; making the written
+    memory visible to another process is the caller's synchronisation (an interprocess event)."""
+    if not o_ptr:
+        raise ValueError("o_ptr must be a device address")
+    _, lse = _fwd_csr(q, k, v, row_ptr, col_idx, seq_lens, scale, out_dtype, None, lse_out,
+                      return_lse, plan, int(o_ptr))
+    return lse
 
 
 def block_sparse_attn_fwd_window(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor,

@@ -163,8 +163,9 @@ class PeerGatherUnavailable(RuntimeError):
 
 
 class PeerGather:
-    """Rank 0's [total_heads, ...] output buffer, written by every rank with copy-engine peer
-    copies.
+    """Rank 0's [total_heads, ...] output buffer, written by every rank, either with copy-engine
+    peer copies of finished chunks (``run``) or directly by each rank's attention kernel
+    (``run_fused``).
 
     Why not NCCL for the overlapped gather: NCCL moves data with kernels, and the attention
     kernel is persistent -- one CTA per SM holding the whole register file and most of shared
@@ -272,6 +273,33 @@ class PeerGather:
         if self.rank != 0:
             self.event.record(self.comm)
             cur.wait_stream(self.comm)
+        dist.barrier(group=self.host)  # every rank has recorded its event
+        if self.rank == 0:
+            for ev in self.peer_events:
+                cur.wait_event(ev)
+
+    def out_ptr(self) -> int:
+        """Device address of this rank's rows ([n_local, ...] starting at its first head) in rank
+        0's buffer, valid on this rank's GPU: rank 0's own memory, or the mapping of it."""
+        s0, _ = shard_range(self.total_heads, self.world, self.rank)
+        base = self.root.data_ptr() if self.rank == 0 else self.remote
+        return base + s0 * self.row_bytes
+
+    def run_fused(self, launch) -> None:
+        """Compute and gather in one step: ``launch(ptr)`` enqueues, on the current stream, the
+        computation of this rank's whole share with its output at device address ``ptr``
+        (``out_ptr()``, e.g. through ``block_sparse_attn_fwd_into``).  On ranks other than 0
+        that address is rank 0's memory, so each output tile crosses NVLink as the kernel's
+        epilogue stores it, overlapped with the rest of the computation tile by tile, and no
+        copy follows.  Ordering is as in ``run``: on return rank 0's current stream waits on
+        every rank's interprocess event, recorded after its kernel."""
+        import torch.distributed as dist
+        cur = torch.cuda.current_stream(self.device)
+        s0, s1 = shard_range(self.total_heads, self.world, self.rank)
+        if s1 > s0:
+            launch(self.out_ptr())
+        if self.rank != 0:
+            self.event.record(cur)
         dist.barrier(group=self.host)  # every rank has recorded its event
         if self.rank == 0:
             for ev in self.peer_events:
