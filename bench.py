@@ -15,14 +15,18 @@ Every line also carries ``mix``: the head-sharded scaling configuration, one B=4
 problem whose heads cycle through window16 / prefix8+window8 / retrieval(2+16), its 128 (batch,
 head) pairs split contiguously across the N ranks (strong scaling: the total work is fixed).  It
 reports the kernel time (max over ranks) and the time until rank 0 holds every head, with each
-rank's heads computed in chunks and every finished chunk copied into rank 0's output while the
-next one computes (copy-engine peer copies over NVLink; NCCL send/recv with --mix-transport nccl),
-and rank 0's bit-exact check of the first and last head of every rank's share.
+rank's output tiles stored straight into rank 0's buffer over NVLink by the kernel's own epilogue
+(the default, ``--mix-transport fused``), or its heads computed in chunks with every finished chunk
+copied into rank 0's output while the next one computes (copy-engine peer copies with
+``--mix-transport copy``, NCCL send/recv with ``--mix-transport nccl``), and rank 0's bit-exact check
+of the first and last head of every rank's share.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload families|mix] [--mix-transport copy|nccl] [--no-mix]
+                    [--workload families|mix|dense] [--mix-transport fused|copy|nccl] [--no-mix]
 
-``--workload mix`` prints the scaling configuration as its own line (with an end-to-end leg).
+``--workload mix`` prints the scaling configuration as its own line (with an end-to-end leg);
+``--workload dense`` prints a comparison line: this kernel on dense causal attention next to torch
+SDPA (cuDNN, flash) and flash_attn 2 on the same inputs.
 
 ``--impl reference`` times the reference's CPU path (the dense-masked fp32 restatement in
 oracle/, the reference having no CPU implementation of its own) on the host cores, rank 0 only.
@@ -555,6 +559,109 @@ def measure_mix(args, rank, world, device, peaks):
     return res, extra
 
 
+DENSE_CASES = [(2, 16, 8192), (1, 8, 32768)]
+DENSE_METRIC = "dense causal attention forward TFLOP/s (4*B*H*D*T(T+1)/2 FLOP per call), D=128 fp16"
+
+
+def run_dense(args, rank, world, local_rank):
+    """``--workload dense``: a comparison point for the roofline fraction.  This kernel runs a
+    dense causal pattern (every block at or below the diagonal: the window family with a window as
+    long as the sequence) next to the dense causal attention of torch's SDPA (cuDNN and flash
+    backends) and of flash_attn 2, on identical inputs.  Those library kernels serve only as
+    comparison points here; nothing in the package calls them.  FLOPs are the exact causal count
+    for every implementation.  Each call is timed alone with CUDA events, L2 flushed before it;
+    the kernel of this build is timed before and after the libraries and reported as the median
+    over both blocks.  Rank 0 alone runs it."""
+    if rank != 0:
+        return 0
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    import usagi_b200 as ub
+    from usagi_b200 import patterns as P
+
+    torch.cuda.set_device(local_rank)
+    device = torch.device("cuda", local_rank)
+    ub.setup(device=str(device))
+    peaks = load_peaks()
+    flush = torch.empty(512 * 1024 * 1024, dtype=torch.uint8, device=device)
+    n = max(10, min(args.steps, 50))
+
+    def time_calls(fn):
+        for _ in range(max(args.warmup, 3)):
+            flush.zero_()
+            fn()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+               for _ in range(n)]
+        for a, b in evs:
+            flush.zero_()
+            a.record()
+            fn()
+            b.record()
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in evs]
+
+    cases = []
+    with ClockSampler(local_rank) as clk:
+        for (b, h, t) in DENSE_CASES:
+            g = torch.Generator().manual_seed(0)
+            q, k, v = [torch.randn((b, h, t, D), generator=g).half().to(device) for _ in range(3)]
+            nqb = t // 128
+            pat = P.window_pattern(b, h, t, window=nqb)
+            rp, ci = pat.row_ptr.to(device), pat.col_idx.to(device)
+            plan = ub.make_plan(pat.row_ptr, pat.col_idx, b, h, t, device=device)
+            o = torch.empty_like(q)
+            lse = torch.empty((b, h, t), device=device, dtype=torch.float32)
+
+            def ours():
+                ub.block_sparse_attn_fwd(q, k, v, rp, ci, None, out=o, lse_out=lse, plan=plan)
+
+            times = {"usagi_b200": time_calls(ours)}
+            ub.check_errors(device)
+            flops = 4.0 * b * h * D * t * (t + 1) / 2
+            res, errors, maxdiff = {}, {}, {}
+            for name, be in (("torch_sdpa_cudnn", SDPBackend.CUDNN_ATTENTION),
+                             ("torch_sdpa_flash", SDPBackend.FLASH_ATTENTION)):
+                try:
+                    with sdpa_kernel([be]):
+                        ref = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+                        times[name] = time_calls(
+                            lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True))
+                    maxdiff[name] = float((ref.float() - o.float()).abs().max())
+                    del ref
+                except Exception as e:  # noqa: BLE001 - a backend missing on this box
+                    errors[name] = f"{type(e).__name__}: {str(e)[:160]}"
+            try:
+                from flash_attn import flash_attn_func
+                qt, kt, vt = (x.transpose(1, 2).contiguous() for x in (q, k, v))
+                ref = flash_attn_func(qt, kt, vt, causal=True)
+                times["flash_attn2"] = time_calls(lambda: flash_attn_func(qt, kt, vt, causal=True))
+                maxdiff["flash_attn2"] = float((ref.transpose(1, 2).float() - o.float()).abs().max())
+                del qt, kt, vt, ref
+            except Exception as e:  # noqa: BLE001
+                errors["flash_attn2"] = f"{type(e).__name__}: {str(e)[:160]}"
+            times["usagi_b200"] += time_calls(ours)
+            for name, ts in times.items():
+                ms = statistics.median(ts)
+                tf = flops / (ms * 1e-3) / 1e12
+                res[name] = {"ms": round(ms, 4), "tflops": round(tf, 1),
+                             "frac_of_peak": round(tf / peaks["bf16_tflops"], 3)}
+            for name, d in maxdiff.items():
+                assert d < 1e-2, (name, d)  # same attention, fp16 outputs
+            cases.append({"B": b, "H": h, "T": t, "D": D, "flops": flops, "results": res,
+                          "max_abs_diff_vs_usagi_b200": maxdiff, "errors": errors})
+            del q, k, v, o, lse
+            torch.cuda.empty_cache()
+    print(json.dumps({
+        "metric": DENSE_METRIC, "unit": "TFLOP/s", "impl": "ours", "workload": "dense",
+        "higher_is_better": True, "n_gpus": 1, "calls_per_case": n, "dtype": "fp16",
+        "data": "synthetic: N(0,1) fp32 from CPU seed 0 in the order q, k, v, cast to fp16",
+        "pattern": "usagi_b200: CSR rows of every block 0..qb (window = T/128); libraries: is_causal",
+        "l2": "flushed (512 MB write) before every timed call",
+        "peak": {"value": peaks["bf16_tflops"], "unit": "TFLOP/s", "source": peaks["source"]},
+        "cases": cases, "clocks": clk.summary()}), flush=True)
+    return 0
+
+
 def run_mix(args, rank, world, local_rank):
     """``--workload mix``: the scaling configuration as its own JSON line (with an end-to-end leg
     through the public API on each rank's share)."""
@@ -840,9 +947,10 @@ def main():
                     help="round-robin item order instead of the balanced work list")
     ap.add_argument("--family", choices=FAMILIES, default=None,
                     help="run one family only (profiling); the JSON line then covers that family")
-    ap.add_argument("--workload", choices=["families", "mix"], default="families",
+    ap.add_argument("--workload", choices=["families", "mix", "dense"], default="families",
                     help="families: the headline 3-family workload (weak scaling); mix: the "
-                         "head-sharded scaling configuration (strong scaling)")
+                         "head-sharded scaling configuration (strong scaling); dense: this "
+                         "kernel on dense causal attention next to library kernels (comparison)")
     ap.add_argument("--quick", action="store_true",
                     help="device-timed region only: no e2e, cpu_baseline or gather (profiling)")
     args = ap.parse_args()
@@ -862,6 +970,8 @@ def main():
         return run_reference(args, rank, world)
     if args.workload == "mix":
         return run_mix(args, rank, world, local_rank)
+    if args.workload == "dense":
+        return run_dense(args, rank, world, local_rank)
 
     import torch.distributed as dist
     import usagi_b200 as ub
